@@ -1,0 +1,363 @@
+#!/usr/bin/env python3
+"""Benchmark of the PRIME moment attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline metric (one JSON line from rank 0): config-2 prefill throughput,
+tokens/s over all GPUs -- B=8 sequences per GPU, H=12 heads, D=64, L=8192, bf16
+q/k/v, fp32 state, per-head lambda log-uniform in [0.99, 0.9999].  A "step" is one
+pma_prefill call over that batch (y and the final state).  The line also carries
+the config-3 decode step (256 sequences x 12 layers x 12 heads, D=64, one launch
+for all layers' heads, 1000 timed steps) under "decode".
+
+Multi-GPU: one process per GPU (torchrun); each rank prefills its own batch x head
+shard with no collective (weak scaling); times are the max over ranks.
+
+--impl reference times the reference's own C99 runtime (c/prime_moment.c, built
+unmodified into oracle/_ref/ by oracle/Makefile) on the host cores, additive mode,
+on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import shutil
+import subprocess
+import sys
+import tempfile
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+PREFILL = dict(B=8, H=12, L=8192, D=64, lam=(0.99, 0.9999), seed=2)
+DECODE = dict(seqs=256, layers=12, H=12, D=64, lam=(0.99, 0.9999), t0=4096, sigma=0.01, seed=3, steps=1000)
+PREFILL_BYTES_PER_TOKHEAD = 8 * 64          # q,k,v in + y out, bf16: 8*D bytes
+PREFILL_FLOP_PER_TOKHEAD = 6 * 64 * 64 + 8 * 64 * 64   # 57,344 (dense-chunk count at C=64)
+DECODE_BYTES_PER_HEADSTEP = 2 * (2 * 64 * 64 + 3 * 64 + 1) * 4 + 3 * 64 * 2 + 64 * 2  # 67,592
+WORKLOAD = ("config2 prefill: B=8 seqs/GPU, H=12, D=64, L=8192, bf16 q/k/v (QK-normed), fp32 state, "
+            "per-head lambda log-U[0.99,0.9999]; step = one pma_prefill (y + final state)")
+
+
+def _peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle samples taken during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        if not shutil.which("nvidia-smi"):
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits", "-lms", "100"],
+                                     stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        time.sleep(0.25)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = sorted(int(r[1]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": int(rows[0][2]), "samples": len(rows),
+                "reasons": reasons}
+
+
+# --------------------------------------------------------------------------- distributed
+def dist_setup():
+    import torch
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, ws: int, device) -> float:
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------- CPU baseline
+def ref_bench_path():
+    p = os.path.join(HERE, "oracle", "_ref", "ref_bench")
+    return p if os.path.exists(p) else None
+
+
+def run_ref(args_list, timeout=600):
+    out = subprocess.run([ref_bench_path(), *map(str, args_list)], capture_output=True, text=True,
+                         timeout=timeout, check=True)
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+def cpu_prefill_sample(target_s: float = 12.0):
+    """Reference C99 prime_prefill (additive, eps=1) on all host cores: tokens/s.
+
+    Calibrates on a short run, then times states x tokens sized for ~target_s."""
+    threads = os.cpu_count() or 1
+    c = PREFILL
+    cal = run_ref(["prefill", threads, c["H"], 256, c["D"], threads])
+    rate = cal["tok_per_s"]
+    L = 2048
+    nstates = max(threads, int(rate * target_s / L))
+    nstates = (nstates + threads - 1) // threads * threads
+    r = run_ref(["prefill", nstates, c["H"], L, c["D"], threads], timeout=int(20 * target_s) + 60)
+    return {"value": r["tok_per_s"], "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"reference c/prime_moment.c prime_prefill (additive, eps=1), {nstates} sequences x "
+                      f"{L} tokens x {c['H']} heads x D={c['D']}, {threads} threads, {r['seconds']:.1f} s"}
+
+
+def cpu_decode_sample(target_s: float = 6.0):
+    """Reference C99 prime_step over seqs x layers states: projected us per config-3 step."""
+    threads = os.cpu_count() or 1
+    c = DECODE
+    total_states = c["seqs"] * c["layers"]
+    cal = run_ref(["decode", threads * 4, c["H"], c["D"], 3, threads])
+    per_state = cal["seconds"] / (3 * threads * 4)
+    nstates = min(total_states, max(threads, int(target_s / max(per_state, 1e-9) / 4)))
+    r = run_ref(["decode", nstates, c["H"], c["D"], 4, threads], timeout=int(20 * target_s) + 60)
+    us = r["us_per_step"] * total_states / nstates
+    return {"value": us, "unit": "us/step", "cores": threads, "kind": "reference",
+            "sample": f"reference c/prime_moment.c prime_step (additive, eps=1), {nstates} of {total_states} "
+                      f"seq x layer states (12 heads each), 4 steps, {threads} threads, scaled to all states"}
+
+
+def run_reference_arm(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    if ref_bench_path() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/ref_bench was not built (needs the "
+                          "reference tree when build() ran)"}))
+        return 0
+    threads = os.cpu_count() or 1
+    vals = []
+    sample = None
+    # each step is a bounded sample of the workload; warmup steps are shorter
+    for i in range(args.warmup + args.steps):
+        r = cpu_prefill_sample(target_s=2.0 if i < args.warmup else 6.0)
+        if i >= args.warmup:
+            vals.append(r["value"])
+            sample = r["sample"]
+    v = sum(vals) / len(vals)
+    dec = cpu_decode_sample(target_s=4.0)
+    line = {"impl": "reference", "metric": "prefill_tok_per_s", "value": v, "unit": "tok/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(PREFILL["B"] * PREFILL["L"] / v * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": PREFILL["B"], "seq_len": PREFILL["L"],
+                       "parallelism": f"host, {threads} threads"},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "decode": {"metric": "decode_step_us", "value": dec["value"], "unit": "us/step",
+                       "higher_is_better": False, "sample": dec["sample"]}}
+    print(json.dumps(line))
+    return 0
+
+
+# --------------------------------------------------------------------------- our arm
+def time_steps(fn, steps, warmup, ws, device, stream):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    barrier(ws)
+    torch.cuda.synchronize(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(ws)
+    torch.cuda.synchronize(device)
+    return e0.elapsed_time(e1) / steps  # ms per step
+
+
+def run_ours(args):
+    import torch
+    ws, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from prime_moment_attention_b200 import _lib, ops, synth
+
+    hbm_peak, tc_peak, peak_kind = _peaks()
+    stream = torch.cuda.current_stream(device)
+    c = PREFILL
+    B, H, L, D = c["B"], c["H"], c["L"], c["D"]
+    q, k, v = synth.make_qkv(B, H, L, D, seed=c["seed"] + 1000 * rank, dtype=torch.bfloat16, device=device)
+    lam = synth.make_lambdas(H, *c["lam"], seed=c["seed"]).to(device)
+    y = torch.empty_like(q)
+    ws_bytes = _lib.load().pma_prefill_workspace_bytes(B, H, L, D, _lib.PMA_BF16)
+    launches_per_step = 3 if ws_bytes else 1
+
+    def step():
+        ops.prefill(q, k, v, lam, y_out=y, return_state=True)
+
+    clocks = ClockSampler(local)
+    for _ in range(args.warmup):
+        step()
+    clocks.start()
+    ms = time_steps(step, args.steps, 0, ws, device, stream)
+    clk = clocks.stop()
+    ms = max_over_ranks(ms, ws, device)
+    tokens = B * L * ws
+    value = tokens / (ms * 1e-3)
+    tokheads = B * L * H
+    algo_bytes = tokheads * PREFILL_BYTES_PER_TOKHEAD
+    algo_flop = tokheads * PREFILL_FLOP_PER_TOKHEAD
+    bw = algo_bytes / (ms * 1e-3) / 1e9
+    tf = algo_flop / (ms * 1e-3) / 1e12
+    roof = {"bound": "hbm", "achieved": round(bw, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(bw / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+            "tensor": {"achieved": round(tf, 1), "peak": tc_peak, "unit": "TFLOP/s", "frac": round(tf / tc_peak, 4)},
+            "timed": "whole pma_prefill call (all its launches), CUDA events on the launching stream",
+            "algorithmic_bytes_per_launch": algo_bytes, "algorithmic_flop_per_launch": algo_flop}
+
+    # ---- e2e through the public API with host buffers
+    e2e_steps = max(1, min(args.steps, 5))
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    yh = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        yy, _ = ops.prefill(qd, kd, vd, lam, return_state=True)
+        yh.copy_(yy, non_blocking=True)
+
+    e2e_ms = max_over_ranks(time_steps(e2e_step, e2e_steps, 1, ws, device, stream), ws, device)
+    h2d = 3 * q.numel() * q.element_size()
+    d2h = y.numel() * y.element_size()
+    del qh, kh, vh, yh, qd, kd, vd
+
+    # ---- decode (config 3)
+    dc = DECODE
+    N, HD = dc["seqs"], dc["layers"] * dc["H"]
+    lam_d = synth.make_lambdas(HD, *dc["lam"], seed=dc["seed"]).to(device)
+    st = synth.make_state(N, HD, dc["D"], lam_d, seed=dc["seed"] + rank, t0=dc["t0"], sigma=dc["sigma"],
+                          device=device)
+    toks = [synth.make_decode_tokens(N, HD, dc["D"], seed=dc["seed"] * 100 + i, device=device) for i in range(8)]
+    yd = torch.empty(N, HD, dc["D"], dtype=torch.bfloat16, device=device)
+    it = [0]
+
+    def dstep():
+        qq, kk, vv = toks[it[0] & 7]
+        it[0] += 1
+        ops.decode_step(qq, kk, vv, lam_d, st, inplace=True, y_out=yd)
+
+    dclk = ClockSampler(local)
+    for _ in range(max(3, args.warmup)):
+        dstep()
+    dclk.start()
+    dms = max_over_ranks(time_steps(dstep, dc["steps"], 0, ws, device, stream), ws, device)
+    dclk_r = dclk.stop()
+    d_bytes = N * HD * DECODE_BYTES_PER_HEADSTEP
+    d_bw = d_bytes / (dms * 1e-3) / 1e9
+    decode = {"metric": "decode_step_us", "value": round(dms * 1e3, 2), "unit": "us/step",
+              "higher_is_better": False, "steps": dc["steps"],
+              "config": {"workload": "config3 decode: 256 seqs x 12 layers x 12 heads per GPU, D=64, bf16 q/k/v, "
+                                     "fp32 state in place, all layers' heads in one launch",
+                         "state_bytes": N * HD * (2 * 64 * 64 + 3 * 64 + 1) * 4, "l2": "state 1.24 GB > L2"},
+              "roofline": {"bound": "hbm", "achieved": round(d_bw, 1), "peak": hbm_peak, "unit": "GB/s",
+                           "frac": round(d_bw / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+                           "algorithmic_bytes_per_launch": d_bytes},
+              "gpu_launches": dc["steps"], "clocks": dclk_r}
+    del st, toks
+
+    line = {"metric": "prefill_tok_per_s", "value": round(value, 1), "unit": "tok/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": B * ws, "seq_len": L,
+                       "parallelism": f"dp{ws} (batch x head shards, no collective)",
+                       "l2": "inputs 403 MB per GPU > 126 MB L2; no flush"},
+            "roofline": roof,
+            "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
+                    "path": "pinned host q,k,v -> H2D -> ops.prefill (C ABI pma_prefill) -> D2H y"},
+            "gpu_launches": args.steps * launches_per_step,
+            "clocks": clk,
+            "decode": decode}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and ref_bench_path():
+        try:
+            line["cpu_baseline"] = cpu_prefill_sample()
+            line["decode"]["cpu_baseline"] = cpu_decode_sample()
+        except Exception as e:  # the baseline must not sink the GPU number
+            line["cpu_baseline"] = {"error": str(e)[:200]}
+    if rank == 0:
+        print(json.dumps(line))
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

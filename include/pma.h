@@ -1,0 +1,180 @@
+/*
+ * pma.h -- C ABI of the B200 (sm_100a) PRIME moment attention hot path.
+ *
+ * Library: prime_moment_attention_b200/libpma.so (nvcc, -gencode arch=compute_100a,code=sm_100a).
+ * Plain C types only: device pointers, sizes, strides, a CUDA stream handle.
+ *
+ * Semantics are those of the reference PyTorch path (paths relative to the
+ * PRIME-Moment-Attention project root).  Per head-state, with decay l in (0,1],
+ * q pre-scaled by 1/sqrt(D) (attention.py:101), for every token t in order:
+ *
+ *     S0 = l S0 + v            Z0 = l Z0 + 1
+ *     S1 = l S1 + k v^T        Z1 = l Z1 + k          (S1[d][e]: d = key index)
+ *     S2 = l S2 + (k*k) v^T    Z2 = l Z2 + k*k
+ *     y  = (S0 + q^T S1 + 0.5 (q*q)^T S2) / max(Z0 + q.Z1 + 0.5 (q*q).Z2, eps)
+ *
+ * The reference names Z0, Z1, Z2 "K0, K1, K2" (attention.py:19-24).
+ *
+ * Conventions
+ *   - Every entry point returns an int status (pma_status); 0 is success.  Argument
+ *     errors are found on the host before anything is launched.  Kernels are
+ *     launched on `stream` (NULL = the legacy default stream) and run
+ *     asynchronously; PMA_ERR_CUDA reports a launch failure.
+ *   - No entry point allocates device memory.  Scratch space is passed in
+ *     (pma_prefill_workspace_bytes says how much).
+ *   - Entry points are re-entrant and hold no global mutable state other than a
+ *     per-device cache of kernel attributes set once.
+ *   - Sequence tensors (q, k, v, y) are [B, H, L, D] with arbitrary element
+ *     strides on B, H, L and a contiguous D axis, so both the reference's
+ *     [B,H,L,D] tensors and its transposed views of [B,L,H,D] projections
+ *     (attention.py:87-89) are accepted without a copy.
+ *   - States are float32, contiguous, in the reference tuple layout
+ *     (attention.py:111-117).
+ */
+#ifndef PMA_H
+#define PMA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PMA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define PMA_API __attribute__((visibility("default")))
+#else
+#define PMA_API
+#endif
+
+/* Same type as cudaStream_t. */
+typedef struct CUstream_st *pma_stream_t;
+
+typedef enum {
+    PMA_OK = 0,
+    PMA_ERR_ARGUMENT = 1,   /* null pointer where one is required, negative size   */
+    PMA_ERR_HEAD_DIM = 2,   /* head_dim not supported by any kernel                */
+    PMA_ERR_DTYPE = 3,      /* element type not supported                          */
+    PMA_ERR_LAYOUT = 4,     /* stride/alignment the kernels cannot address         */
+    PMA_ERR_WORKSPACE = 5,  /* workspace missing or smaller than required          */
+    PMA_ERR_CUDA = 6,       /* a CUDA runtime call or kernel launch failed         */
+    PMA_ERR_DEVICE = 7      /* current device is not sm_100 (B200 class)           */
+} pma_status;
+
+typedef enum {
+    PMA_F32 = 0,
+    PMA_BF16 = 1
+} pma_dtype;
+
+/* A [B, H, L, D] device tensor with element strides; D is contiguous. */
+typedef struct {
+    void *data;
+    int32_t dtype;     /* pma_dtype */
+    int64_t stride_b;
+    int64_t stride_h;
+    int64_t stride_l;
+} pma_seq_tensor;
+
+/* Six contiguous float32 device arrays holding B x H head-states.
+ * Reference tuple (S0, S1, S2, K0, K1, K2) of attention.py:111-117. */
+typedef struct {
+    float *S0;   /* [B, H, D]                       */
+    float *S1;   /* [B, H, D, D]  row = key index   */
+    float *S2;   /* [B, H, D, D]  row = key index   */
+    float *Z0;   /* [B, H]   (reference K0 [B,H,1]) */
+    float *Z1;   /* [B, H, D]                       */
+    float *Z2;   /* [B, H, D]                       */
+} pma_state;
+
+/* ABI version (PMA_ABI_VERSION of the built library). */
+PMA_API int pma_version(void);
+
+/* Static text for a status code. */
+PMA_API const char *pma_status_string(int status);
+
+/* Floats in one head-state: 2*D*D + 3*D + 1 (c/prime_moment.h:17 states the
+ * same count for the reference's C runtime). */
+PMA_API size_t pma_state_floats(int D);
+
+/* Head dims the kernels support for each input dtype: writes up to `cap`
+ * values into `dims` and returns how many there are. */
+PMA_API int pma_supported_head_dims(int dtype, int *dims, int cap);
+
+/*
+ * Bytes of scratch pma_prefill needs for this problem (0 if none).
+ * Replaces nothing in the reference; the reference allocates through ATen.
+ */
+PMA_API size_t pma_prefill_workspace_bytes(int B, int H, int L, int D, int dtype);
+
+/*
+ * Chunked prefill of L tokens for B x H head-states.
+ *
+ * Replaces chunked_prime_ssd_core (src/prime_moment_attention/chunked_ssd.py:48-184)
+ * and the dense short-sequence branch of PrimeMomentAttention.forward
+ * (attention.py:160-202); also the sequential prime_prefill_cpp
+ * (prime_cpp_kernel.cpp:6-47) and C prime_prefill (c/prime_moment.c:332-352).
+ *
+ *   q, k, v     [B,H,L,D], all the same dtype (F32 or BF16); q pre-scaled.
+ *   lambda      device float array; head h of batch row b uses
+ *               lambda[b * lambda_stride_b + h] (stride 0: one decay per head).
+ *   state_in    NULL = zero initial state (the reference's state=None), else the
+ *               incoming state.  Unlike chunked_ssd.py:129-137 any B, H, L work.
+ *   state_out   NULL = final state not wanted (return_state=False); else receives
+ *               the state after token L-1.  May alias state_in.
+ *   eps         denominator clamp (1.0 in the reference module, attention.py:51).
+ *   y           [B,H,L,D] output, F32 or BF16 (any strides, D contiguous); NULL
+ *               computes only state_out (the state-only pass used by sequence
+ *               sharding).
+ *   workspace   device scratch of at least pma_prefill_workspace_bytes(...).
+ *
+ * F32 inputs are computed with float32 arithmetic throughout (CUDA cores).
+ * BF16 inputs with D = 64 run on tcgen05 tensor cores: bf16 operands, float32
+ * accumulation, float32 state.  L == 0 copies state_in to state_out.
+ */
+PMA_API int pma_prefill(int B, int H, int L, int D,
+                const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                const float *lambda, int64_t lambda_stride_b,
+                const pma_state *state_in, const pma_state *state_out,
+                float eps, const pma_seq_tensor *y,
+                void *workspace, size_t workspace_bytes, pma_stream_t stream);
+
+/*
+ * One recurrent decode step for N x H head-states (N = batch rows, or
+ * sequences x layers when all layers' heads are batched in one launch).
+ *
+ * Replaces the L == 1 branch of PrimeMomentAttention.forward
+ * (attention.py:120-143); also prime_step_evict_update_cpp followed by
+ * prime_query_step_cpp (prime_cpp_kernel.cpp:84-117) and the additive mode of
+ * prime_step (c/prime_moment.c:274-312).
+ *
+ *   q, k, v, y  [N,H,D] tensors described as pma_seq_tensor with L = 1
+ *               (stride_b = row stride, stride_h = head stride, stride_l ignored).
+ *   lambda      lambda[n * lambda_stride_n + h].
+ *   state_in    required; state_out required; they may be the same arrays
+ *               (in-place update) or disjoint (functional update, as the
+ *               reference returns new tensors).
+ */
+PMA_API int pma_decode_step(int N, int H, int D,
+                    const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                    const float *lambda, int64_t lambda_stride_n,
+                    const pma_state *state_in, const pma_state *state_out,
+                    float eps, const pma_seq_tensor *y, pma_stream_t stream);
+
+/*
+ * Segment carry: P <- lambda^len * P + T for B x H head-states, elementwise over
+ * all six components.  len = tokens in the segment that produced T.
+ * This is the associative step of the reference's inter-chunk scan
+ * (chunked_ssd.py:113-126, evaluated there as a dense [nc x nc] matmul); here it
+ * joins sequence shards computed on different GPUs.
+ */
+PMA_API int pma_state_combine(int B, int H, int D, const float *lambda, int64_t lambda_stride_b,
+                      int64_t len, const pma_state *T, const pma_state *P,
+                      pma_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PMA_H */

@@ -1,0 +1,283 @@
+// pma_capi.cu -- the extern "C" entry points declared in include/pma.h:
+// argument validation on the host, planning (kernel, chunk, segments) and launch.
+#include <mutex>
+
+#include "prefill.cuh"
+
+using namespace pma;
+
+namespace {
+
+struct DevInfo {
+    int sms = 0;
+    int major = 0;
+    bool valid = false;
+};
+
+inline int d_ok(const DevInfo &d) { return d.major == 10 ? PMA_OK : PMA_ERR_DEVICE; }
+
+constexpr int kMaxDevices = 64;
+DevInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DevInfo *out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return PMA_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!g_dev[dev].valid) {
+        DevInfo d;
+        if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return PMA_ERR_CUDA;
+        if (cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return PMA_ERR_CUDA;
+        d.valid = true;
+        g_dev[dev] = d;
+    }
+    *out = g_dev[dev];
+    return d_ok(*out);
+}
+
+bool supported_d(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
+bool supported_dtype(int t) { return t == PMA_F32 || t == PMA_BF16; }
+size_t esize(int t) { return t == PMA_F32 ? 4 : 2; }
+
+// Each row of D elements must start on a 16-byte boundary (vector loads, TMA).
+int check_seq(const pma_seq_tensor *t, bool use_l) {
+    if (!t || !t->data) return PMA_ERR_ARGUMENT;
+    if (!supported_dtype(t->dtype)) return PMA_ERR_DTYPE;
+    const int64_t step = 16 / (int64_t)esize(t->dtype);
+    if (reinterpret_cast<uintptr_t>(t->data) % 16) return PMA_ERR_LAYOUT;
+    if (t->stride_b % step || t->stride_h % step || (use_l && t->stride_l % step)) return PMA_ERR_LAYOUT;
+    if (t->stride_b < 0 || t->stride_h < 0 || (use_l && t->stride_l < 0)) return PMA_ERR_LAYOUT;
+    return PMA_OK;
+}
+
+int check_state(const pma_state *s) {
+    if (!s || !s->S0 || !s->S1 || !s->S2 || !s->Z0 || !s->Z1 || !s->Z2) return PMA_ERR_ARGUMENT;
+    const uintptr_t a[6] = {(uintptr_t)s->S0, (uintptr_t)s->S1, (uintptr_t)s->S2,
+                            (uintptr_t)s->Z1, (uintptr_t)s->Z2, 0};
+    for (int i = 0; i < 6; ++i)
+        if (a[i] % 16) return PMA_ERR_LAYOUT;
+    if ((uintptr_t)s->Z0 % 4) return PMA_ERR_LAYOUT;
+    return PMA_OK;
+}
+
+Seq seq_of(const pma_seq_tensor *t) { return Seq{t->data, t->stride_b, t->stride_h, t->stride_l}; }
+SeqOut seqout_of(const pma_seq_tensor *t) {
+    return t ? SeqOut{t->data, t->stride_b, t->stride_h, t->stride_l} : SeqOut{nullptr, 0, 0, 0};
+}
+StateRef user_ref(const pma_state *s) {
+    StateRef r{};
+    if (s) r.user = *s;
+    r.packed = nullptr;
+    r.slots = 1;
+    return r;
+}
+StateRef packed_ref(float *ws, int slots) {
+    StateRef r{};
+    r.packed = ws;
+    r.slots = slots;
+    return r;
+}
+
+struct Plan {
+    bool tc = false;
+    int chunk = 64;
+    int nseg = 1;
+    int seg_len = 0;
+    size_t ws_bytes = 0;
+};
+
+Plan make_plan(int B, int H, int L, int D, int dtype, int sms) {
+    Plan p;
+    p.tc = tc_supported(D, dtype);
+    p.chunk = p.tc ? TC_CHUNK : simt_chunk(D);
+    const int BH = B * H;
+    const int nchunks = (L + p.chunk - 1) / p.chunk;
+    // CTAs resident per SM: SIMT D<=64 fits two, D=128 and the tensor-core kernel one.
+    const int per_sm = (!p.tc && D <= 64) ? 2 : 1;
+    const long target = (long)sms * per_sm;
+    int nseg = 1;
+    if (BH > 0 && BH < target) nseg = (int)((target + BH - 1) / BH);
+    if (nseg > nchunks) nseg = nchunks;
+    if (nseg < 1) nseg = 1;
+    const int seg_chunks = (nchunks + nseg - 1) / nseg;
+    p.nseg = seg_chunks > 0 ? (nchunks + seg_chunks - 1) / seg_chunks : 1;
+    p.seg_len = seg_chunks * p.chunk;
+    if (p.nseg > 1) p.ws_bytes = (size_t)BH * p.nseg * state_floats(D) * sizeof(float);
+    return p;
+}
+
+cudaError_t launch_prefill(const Plan &pl, const PrefillParams &p, int D, int idt, int ydt, dim3 grid,
+                           cudaStream_t st) {
+    return pl.tc ? launch_prefill_tc(p, ydt, grid, st) : launch_prefill_simt(p, D, idt, ydt, grid, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int pma_version(void) { return PMA_ABI_VERSION; }
+
+const char *pma_status_string(int status) {
+    switch (status) {
+        case PMA_OK: return "ok";
+        case PMA_ERR_ARGUMENT: return "invalid argument (null pointer or negative size)";
+        case PMA_ERR_HEAD_DIM: return "unsupported head_dim (supported: 16, 32, 64, 128)";
+        case PMA_ERR_DTYPE: return "unsupported dtype (float32 or bfloat16)";
+        case PMA_ERR_LAYOUT: return "unsupported layout (rows must start on 16-byte boundaries, head dim contiguous)";
+        case PMA_ERR_WORKSPACE: return "workspace missing or too small";
+        case PMA_ERR_CUDA: return "CUDA runtime error";
+        case PMA_ERR_DEVICE: return "current device is not sm_100 (B200 class)";
+        default: return "unknown status";
+    }
+}
+
+size_t pma_state_floats(int D) { return D > 0 ? state_floats(D) : 0; }
+
+int pma_supported_head_dims(int dtype, int *dims, int cap) {
+    static const int all[4] = {16, 32, 64, 128};
+    if (!supported_dtype(dtype)) return 0;
+    for (int i = 0; i < 4 && i < cap; ++i)
+        if (dims) dims[i] = all[i];
+    return 4;
+}
+
+size_t pma_prefill_workspace_bytes(int B, int H, int L, int D, int dtype) {
+    if (B <= 0 || H <= 0 || L <= 0 || !supported_d(D) || !supported_dtype(dtype)) return 0;
+    DevInfo di;
+    if (device_info(&di) != PMA_OK) return 0;
+    return make_plan(B, H, L, D, dtype, di.sms).ws_bytes;
+}
+
+int pma_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                const pma_seq_tensor *v, const float *lambda, int64_t lambda_stride_b, const pma_state *state_in,
+                const pma_state *state_out, float eps, const pma_seq_tensor *y, void *workspace,
+                size_t workspace_bytes, pma_stream_t stream) {
+    if (B < 0 || H <= 0 || L < 0 || !lambda || lambda_stride_b < 0) return PMA_ERR_ARGUMENT;
+    if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
+    int rc;
+    if ((rc = check_seq(q, true)) || (rc = check_seq(k, true)) || (rc = check_seq(v, true))) return rc;
+    if (q->dtype != k->dtype || q->dtype != v->dtype) return PMA_ERR_DTYPE;
+    if (y && (rc = check_seq(y, true))) return rc;
+    if (state_in && (rc = check_state(state_in))) return rc;
+    if (state_out && (rc = check_state(state_out))) return rc;
+    DevInfo di;
+    if ((rc = device_info(&di))) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int BH = B * H;
+    if (BH == 0) return PMA_OK;
+
+    if (L == 0) {  // nothing consumed: final state = incoming state
+        if (!state_out) return PMA_OK;
+        const size_t DD = (size_t)D * D;
+        float *dst[6] = {state_out->S0, state_out->S1, state_out->S2, state_out->Z0, state_out->Z1, state_out->Z2};
+        const float *src[6] = {state_in ? state_in->S0 : nullptr, state_in ? state_in->S1 : nullptr,
+                               state_in ? state_in->S2 : nullptr, state_in ? state_in->Z0 : nullptr,
+                               state_in ? state_in->Z1 : nullptr, state_in ? state_in->Z2 : nullptr};
+        const size_t n[6] = {BH * (size_t)D, BH * DD, BH * DD, (size_t)BH, BH * (size_t)D, BH * (size_t)D};
+        for (int i = 0; i < 6; ++i) {
+            cudaError_t e = src[i] ? (src[i] == dst[i] ? cudaSuccess
+                                                        : cudaMemcpyAsync(dst[i], src[i], n[i] * 4,
+                                                                          cudaMemcpyDeviceToDevice, st))
+                                   : cudaMemsetAsync(dst[i], 0, n[i] * 4, st);
+            if (e != cudaSuccess) return PMA_ERR_CUDA;
+        }
+        return PMA_OK;
+    }
+
+    const Plan pl = make_plan(B, H, L, D, q->dtype, di.sms);
+    if (pl.ws_bytes && (!workspace || workspace_bytes < pl.ws_bytes)) return PMA_ERR_WORKSPACE;
+    if (pl.ws_bytes && reinterpret_cast<uintptr_t>(workspace) % 16) return PMA_ERR_WORKSPACE;
+    if (!y && !state_out) return PMA_OK;  // nothing requested
+    const int ydt = y ? y->dtype : PMA_F32;
+
+    PrefillParams p{};
+    p.B = B;
+    p.H = H;
+    p.L = L;
+    p.seg_len = pl.seg_len;
+    p.q = seq_of(q);
+    p.k = seq_of(k);
+    p.v = seq_of(v);
+    p.y = seqout_of(y);
+    p.lambda = lambda;
+    p.lam_sb = lambda_stride_b;
+    p.eps = eps;
+
+    cudaError_t e;
+    if (pl.nseg == 1) {
+        p.in = user_ref(state_in);
+        p.out = user_ref(state_out);
+        p.state_only = 0;
+        e = launch_prefill(pl, p, D, q->dtype, ydt, dim3(BH, 1), st);
+        return e == cudaSuccess ? PMA_OK : PMA_ERR_CUDA;
+    }
+
+    float *ws = reinterpret_cast<float *>(workspace);
+    // 1. each segment's own state from zero (the last one only when no y is wanted)
+    PrefillParams ps = p;
+    ps.y = SeqOut{nullptr, 0, 0, 0};
+    ps.in = user_ref(nullptr);
+    ps.out = packed_ref(ws, pl.nseg);
+    ps.state_only = 1;
+    const int nstate = y ? pl.nseg - 1 : pl.nseg;
+    e = launch_prefill(pl, ps, D, q->dtype, ydt, dim3(BH, nstate), st);
+    if (e != cudaSuccess) return PMA_ERR_CUDA;
+    // 2. in-place prefix: state entering every segment (and the final state if no y)
+    e = launch_segment_prefix(BH, H, D, pl.nseg, pl.seg_len, L, ws, user_ref(state_in),
+                              y ? user_ref(nullptr) : user_ref(state_out), lambda, lambda_stride_b, st);
+    if (e != cudaSuccess) return PMA_ERR_CUDA;
+    if (!y) return PMA_OK;
+    // 3. full pass, every segment starting from its carried state
+    p.in = packed_ref(ws, pl.nseg);
+    p.out = user_ref(state_out);
+    p.state_only = 0;
+    e = launch_prefill(pl, p, D, q->dtype, ydt, dim3(BH, pl.nseg), st);
+    return e == cudaSuccess ? PMA_OK : PMA_ERR_CUDA;
+}
+
+int pma_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                    const float *lambda, int64_t lambda_stride_n, const pma_state *state_in,
+                    const pma_state *state_out, float eps, const pma_seq_tensor *y, pma_stream_t stream) {
+    if (N < 0 || H <= 0 || !lambda || lambda_stride_n < 0) return PMA_ERR_ARGUMENT;
+    if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
+    int rc;
+    if ((rc = check_seq(q, false)) || (rc = check_seq(k, false)) || (rc = check_seq(v, false)) ||
+        (rc = check_seq(y, false)))
+        return rc;
+    if (q->dtype != k->dtype || q->dtype != v->dtype) return PMA_ERR_DTYPE;
+    if ((rc = check_state(state_in)) || (rc = check_state(state_out))) return rc;
+    DevInfo di;
+    if ((rc = device_info(&di))) return rc;
+    if (N == 0) return PMA_OK;
+    if ((long)N * H > (1L << 30)) return PMA_ERR_ARGUMENT;
+    DecodeParams p{};
+    p.N = N;
+    p.H = H;
+    p.q = seq_of(q);
+    p.k = seq_of(k);
+    p.v = seq_of(v);
+    p.y = seqout_of(y);
+    p.lambda = lambda;
+    p.lam_sn = lambda_stride_n;
+    p.in = *state_in;
+    p.out = *state_out;
+    p.eps = eps;
+    cudaError_t e = launch_decode(p, D, q->dtype, y->dtype, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? PMA_OK : PMA_ERR_CUDA;
+}
+
+int pma_state_combine(int B, int H, int D, const float *lambda, int64_t lambda_stride_b, int64_t len,
+                      const pma_state *T, const pma_state *P, pma_stream_t stream) {
+    if (B < 0 || H <= 0 || !lambda || lambda_stride_b < 0 || len < 0) return PMA_ERR_ARGUMENT;
+    if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
+    int rc;
+    if ((rc = check_state(T)) || (rc = check_state(P))) return rc;
+    DevInfo di;
+    if ((rc = device_info(&di))) return rc;
+    if (B == 0) return PMA_OK;
+    cudaError_t e = launch_state_combine(B, H, D, lambda, lambda_stride_b, len, *T, *P,
+                                         reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? PMA_OK : PMA_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,101 @@
+// pma_common.cuh -- shared device/host helpers for the PRIME moment attention kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/pma.h"
+
+namespace pma {
+
+// ---------------------------------------------------------------------------
+// Element access for the two input/output types (float32, bfloat16).
+// ---------------------------------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+    static __device__ __forceinline__ float to_f(float x) { return x; }
+    static __device__ __forceinline__ float from_f(float x) { return x; }
+};
+template <> struct Elem<__nv_bfloat16> {
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+
+// Load 4 consecutive elements (16 B for float, 8 B for bf16) as float4.
+__device__ __forceinline__ float4 load4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ float4 load4(const __nv_bfloat16 *p) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162 *>(&u.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162 *>(&u.y);
+    const float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+    return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+__device__ __forceinline__ void store4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+__device__ __forceinline__ void store4(__nv_bfloat16 *p, float4 v) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t *>(&a);
+    u.y = *reinterpret_cast<uint32_t *>(&b);
+    *reinterpret_cast<uint2 *>(p) = u;
+}
+
+// Streaming (evict-first) float4 load/store for state that is touched once per step.
+__device__ __forceinline__ float4 ldcs4(const float *p) { return __ldcs(reinterpret_cast<const float4 *>(p)); }
+__device__ __forceinline__ void stcs4(float *p, float4 v) { __stcs(reinterpret_cast<float4 *>(p), v); }
+
+__device__ __forceinline__ float4 fma4(float a, float4 x, float4 y) {
+    return make_float4(fmaf(a, x.x, y.x), fmaf(a, x.y, y.y), fmaf(a, x.z, y.z), fmaf(a, x.w, y.w));
+}
+__device__ __forceinline__ float4 scale4(float a, float4 x) { return make_float4(a * x.x, a * x.y, a * x.z, a * x.w); }
+
+// ---------------------------------------------------------------------------
+// Kernel-side views of the ABI structs.
+// ---------------------------------------------------------------------------
+struct Seq {                 // [B,H,L,D] with element strides, D contiguous
+    const void *p;
+    int64_t sb, sh, sl;
+};
+struct SeqOut {
+    void *p;
+    int64_t sb, sh, sl;
+};
+
+// Pointers to one head-state.
+struct HeadPtrs {
+    float *S0, *S1, *S2, *Z0, *Z1, *Z2;
+};
+
+// Either the user's six-array state (index bh) or a packed scratch layout
+// [bh][slot][F] with F = 2D^2 + 3D + 1 ordered S1 | S2 | S0 | Z1 | Z2 | Z0.
+struct StateRef {
+    pma_state user;      // used when packed == nullptr and user.S1 != nullptr
+    float *packed;
+    int slots;           // packed slots per head-state
+    __host__ __device__ bool present() const { return packed != nullptr || user.S1 != nullptr; }
+    __device__ __forceinline__ HeadPtrs at(int bh, int slot, int D) const {
+        HeadPtrs r;
+        if (packed) {
+            const size_t F = 2 * (size_t)D * D + 3 * (size_t)D + 1;
+            float *b = packed + ((size_t)bh * slots + slot) * F;
+            r.S1 = b;
+            r.S2 = b + (size_t)D * D;
+            r.S0 = b + 2 * (size_t)D * D;
+            r.Z1 = r.S0 + D;
+            r.Z2 = r.Z1 + D;
+            r.Z0 = r.Z2 + D;
+        } else {
+            r.S0 = user.S0 + (size_t)bh * D;
+            r.S1 = user.S1 + (size_t)bh * D * D;
+            r.S2 = user.S2 + (size_t)bh * D * D;
+            r.Z0 = user.Z0 + bh;
+            r.Z1 = user.Z1 + (size_t)bh * D;
+            r.Z2 = user.Z2 + (size_t)bh * D;
+        }
+        return r;
+    }
+};
+
+__host__ __device__ constexpr size_t state_floats(int D) { return 2 * (size_t)D * D + 3 * (size_t)D + 1; }
+
+}  // namespace pma

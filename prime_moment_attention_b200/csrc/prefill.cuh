@@ -1,0 +1,47 @@
+// prefill.cuh -- parameters and launchers shared by the prefill kernels.
+#pragma once
+
+#include "pma_common.cuh"
+
+namespace pma {
+
+// One launch processes gridDim.y segments of seg_len tokens for each of
+// gridDim.x = B*H head-states.  Segment s of head-state bh covers tokens
+// [s*seg_len, min((s+1)*seg_len, L)).
+struct PrefillParams {
+    int B, H, L;
+    int seg_len;          // multiple of the kernel's chunk
+    Seq q, k, v;
+    SeqOut y;             // y.p == nullptr: no output rows
+    const float *lambda;
+    int64_t lam_sb;
+    StateRef in;          // state entering each segment (packed: slot = segment); absent = zero
+    StateRef out;         // user: final state (last segment only); packed: slot = segment
+    float eps;
+    int state_only;       // 1: skip the readout, start every segment from zero, write its state to `out`
+};
+
+struct DecodeParams {
+    int N, H;
+    Seq q, k, v;            // [N,H,D] (stride_l unused)
+    SeqOut y;
+    const float *lambda;
+    int64_t lam_sn;
+    pma_state in, out;
+    float eps;
+};
+
+cudaError_t launch_decode(const DecodeParams &p, int D, int idt, int ydt, cudaStream_t s);
+cudaError_t launch_prefill_simt(const PrefillParams &p, int D, int idt, int ydt, dim3 grid, cudaStream_t st);
+int simt_chunk(int D);
+cudaError_t launch_segment_prefix(int BH, int H, int D, int nseg, int seg_len, int L, float *ws, const StateRef &in,
+                                  const StateRef &final_out, const float *lambda, int64_t lam_sb, cudaStream_t st);
+cudaError_t launch_state_combine(int B, int H, int D, const float *lambda, int64_t lam_sb, int64_t len,
+                                 const pma_state &T, const pma_state &P, cudaStream_t st);
+
+// tcgen05 tensor-core prefill (bf16 inputs, D = 64).
+constexpr int TC_CHUNK = 128;
+bool tc_supported(int D, int idt);
+cudaError_t launch_prefill_tc(const PrefillParams &p, int ydt, dim3 grid, cudaStream_t st);
+
+}  // namespace pma

@@ -1,0 +1,204 @@
+"""Torch-facing wrappers of the C ABI: prefill, decode_step, state_combine.
+
+Tensors stay on the GPU; every call goes through libpma.so on the current CUDA
+stream.  Inputs that are not CUDA tensors raise (no CPU fallback).
+
+State tuples use the reference layout (src/prime_moment_attention/attention.py:111-117):
+(S0[B,H,D], S1[B,H,D,D], S2[B,H,D,D], K0[B,H,1], K1[B,H,D], K2[B,H,D]), float32.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence, Tuple, Union
+
+import torch
+
+from . import _lib
+
+StateTuple = Tuple[torch.Tensor, ...]
+Decay = Union[float, Sequence[float], torch.Tensor]
+
+_DT = {torch.float32: _lib.PMA_F32, torch.bfloat16: _lib.PMA_BF16}
+_lam_cache: dict = {}
+
+
+def _require_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = None
+    for t in ts:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise RuntimeError("prime_moment_attention_b200 runs on CUDA tensors only (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _seq_ok(t: torch.Tensor) -> bool:
+    step = 16 // t.element_size()
+    return (t.stride(-1) == 1 and t.data_ptr() % 16 == 0
+            and all(s % step == 0 and s >= 0 for s in t.stride()[:-1]))
+
+
+def _seq(t: torch.Tensor, four_d: bool = True) -> Tuple[_lib.SeqTensor, torch.Tensor]:
+    """pma_seq_tensor for a [B,H,L,D] (or [N,H,D]) tensor, copying only if the
+    kernels cannot address its layout."""
+    if t.dtype not in _DT:
+        raise TypeError(f"unsupported dtype {t.dtype}: float32 or bfloat16")
+    if not _seq_ok(t):
+        t = t.contiguous()
+    if four_d:
+        sb, sh, sl, _ = t.stride()
+    else:
+        sb, sh, _ = t.stride()
+        sl = 0
+    return _lib.SeqTensor(t.data_ptr(), _DT[t.dtype], sb, sh, sl), t
+
+
+def _state(st: StateTuple, B: int, H: int, D: int, name: str) -> Tuple[_lib.State, StateTuple]:
+    if len(st) != 6:
+        raise ValueError(f"{name}: expected a 6-tuple (S0, S1, S2, K0, K1, K2)")
+    shapes = [(B, H, D), (B, H, D, D), (B, H, D, D), (B, H, 1), (B, H, D), (B, H, D)]
+    out = []
+    for i, (t, shp) in enumerate(zip(st, shapes)):
+        if tuple(t.shape) != shp:
+            if i == 3 and t.numel() == B * H:
+                t = t.reshape(B, H, 1)
+            else:
+                raise ValueError(f"{name}[{i}] has shape {tuple(t.shape)}, expected {shp}")
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.data_ptr() % 16:
+            t = t.to(torch.float32).contiguous()
+        out.append(t)
+    return _lib.State(*[t.data_ptr() for t in out]), tuple(out)
+
+
+def new_state(B: int, H: int, D: int, device, zero: bool = True) -> StateTuple:
+    mk = torch.zeros if zero else torch.empty
+    return (mk(B, H, D, device=device), mk(B, H, D, D, device=device), mk(B, H, D, D, device=device),
+            mk(B, H, 1, device=device), mk(B, H, D, device=device), mk(B, H, D, device=device))
+
+
+def lambda_tensor(decay: Decay, B: int, H: int, device) -> Tuple[torch.Tensor, int]:
+    """Device float32 decay table and its batch stride: scalar or [H] -> ([H], 0), [B,H] -> ([B*H], H)."""
+    if isinstance(decay, torch.Tensor):
+        lam = decay.detach().to(device=device, dtype=torch.float32)
+    else:
+        if isinstance(decay, (int, float)):
+            key = (str(device), H, float(decay))
+            t = _lam_cache.get(key)
+            if t is None:
+                t = torch.full((H,), float(decay), dtype=torch.float32, device=device)
+                _lam_cache[key] = t
+            return t, 0
+        lam = torch.tensor(list(decay), dtype=torch.float32, device=device)
+    if lam.dim() == 0:
+        lam = lam.expand(H)
+    if lam.shape == (H,):
+        return lam.contiguous(), 0
+    if lam.shape == (B, H):
+        return lam.contiguous().reshape(B * H), H
+    raise ValueError(f"decay must be a scalar, [H] or [B,H]; got shape {tuple(lam.shape)}")
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
+            state: Optional[StateTuple] = None, eps: float = 1.0, return_state: bool = True,
+            out_dtype: Optional[torch.dtype] = None, y_out: Optional[torch.Tensor] = None,
+            want_y: bool = True):
+    """Chunked prefill over q, k, v [B,H,L,D] (q pre-scaled by 1/sqrt(D)).
+
+    Returns (y [B,H,L,D] or None, final state or None).  `y_out` may be a
+    preallocated [B,H,L,D] view with any strides (e.g. a transpose of [B,L,H,D]).
+    `want_y=False` runs the state-only pass."""
+    dev = _require_cuda(q, k, v)
+    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f"q, k, v must share one [B,H,L,D] shape; got {tuple(q.shape)}, {tuple(k.shape)}, "
+                         f"{tuple(v.shape)}")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k, v must share one dtype")
+    B, H, L, D = q.shape
+    L_ = _lib.load()
+    qs, q = _seq(q)
+    ks, k = _seq(k)
+    vs, v = _seq(v)
+    lam, lam_sb = lambda_tensor(decay, B, H, dev)
+    st_in = None
+    if state is not None:
+        st_in_c, state = _state(state, B, H, D, "state")
+        st_in = ctypes.byref(st_in_c)
+    st_out_t = new_state(B, H, D, dev, zero=False) if return_state else None
+    st_out = ctypes.byref(_lib.State(*[t.data_ptr() for t in st_out_t])) if return_state else None
+    y = None
+    ys = None
+    if want_y:
+        if y_out is not None:
+            if tuple(y_out.shape) != (B, H, L, D) or not _seq_ok(y_out):
+                raise ValueError("y_out must be a [B,H,L,D] tensor with a contiguous, 16-byte aligned last axis")
+            y = y_out
+        else:
+            y = torch.empty(B, H, L, D, dtype=out_dtype or q.dtype, device=dev)
+        ys_c, _ = _seq(y)
+        ys = ctypes.byref(ys_c)
+    ws_bytes = L_.pma_prefill_workspace_bytes(B, H, L, D, _DT[q.dtype])
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    rc = L_.pma_prefill(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(), lam_sb,
+                        st_in, st_out, float(eps), ys, ws.data_ptr() if ws is not None else None, ws_bytes,
+                        _stream(dev))
+    _lib.check("pma_prefill", rc)
+    return y, st_out_t
+
+
+def decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay, state: StateTuple,
+                eps: float = 1.0, inplace: bool = False, out_dtype: Optional[torch.dtype] = None,
+                y_out: Optional[torch.Tensor] = None):
+    """One recurrent step: q, k, v [N,H,D] -> (y [N,H,D], new state).
+
+    With inplace=True the given state tensors are updated and returned (they must
+    already be contiguous float32); otherwise fresh tensors are returned and the
+    input state is left untouched, as in the reference (attention.py:126-132)."""
+    dev = _require_cuda(q, k, v)
+    if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must share one [N,H,D] shape")
+    N, H, D = q.shape
+    L_ = _lib.load()
+    qs, q = _seq(q, False)
+    ks, k = _seq(k, False)
+    vs, v = _seq(v, False)
+    lam, lam_sn = lambda_tensor(decay, N, H, dev)
+    st_in_c, st_in_t = _state(state, N, H, D, "state")
+    if inplace:
+        if any(a is not b for a, b in zip(st_in_t, state)) and not all(
+                a.data_ptr() == b.data_ptr() for a, b in zip(st_in_t, state)):
+            raise ValueError("inplace=True needs contiguous float32 state tensors")
+        st_out_t = st_in_t
+    else:
+        st_out_t = new_state(N, H, D, dev, zero=False)
+    st_out_c = _lib.State(*[t.data_ptr() for t in st_out_t])
+    y = y_out if y_out is not None else torch.empty(N, H, D, dtype=out_dtype or q.dtype, device=dev)
+    ys, y2 = _seq(y, False)
+    if y2 is not y:
+        raise ValueError("y_out must have a contiguous, 16-byte aligned last axis")
+    rc = L_.pma_decode_step(N, H, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(), lam_sn,
+                            ctypes.byref(st_in_c), ctypes.byref(st_out_c), float(eps), ctypes.byref(ys),
+                            _stream(dev))
+    _lib.check("pma_decode_step", rc)
+    return y, st_out_t
+
+
+def state_combine(T: StateTuple, P: StateTuple, decay: Decay, length: int) -> StateTuple:
+    """P <- decay^length * P + T in place (P must be contiguous float32); returns P."""
+    dev = _require_cuda(T[1], P[1])
+    B, H, D = P[0].shape
+    L_ = _lib.load()
+    Tc, T = _state(T, B, H, D, "T")
+    Pc, P2 = _state(P, B, H, D, "P")
+    if any(a.data_ptr() != b.data_ptr() for a, b in zip(P2, P)):
+        raise ValueError("P must be contiguous float32 (it is updated in place)")
+    lam, lam_sb = lambda_tensor(decay, B, H, dev)
+    rc = L_.pma_state_combine(B, H, D, lam.data_ptr(), lam_sb, int(length), ctypes.byref(Tc), ctypes.byref(Pc),
+                              _stream(dev))
+    _lib.check("pma_state_combine", rc)
+    return P

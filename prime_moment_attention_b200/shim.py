@@ -1,0 +1,44 @@
+"""install()/uninstall(): route the reference PrimeMomentAttention onto the CUDA kernels.
+
+`install()` replaces PrimeMomentAttention.forward of the reference package
+(src/prime_moment_attention/attention.py:77-210) by attention.moment_forward,
+which keeps the reference's projection / QK-norm / scale code and sends all three
+L branches to libpma.so.  The state tuple format is unchanged, so
+PrimeMomentCache and PrimeForCausalLM (model.py:101-120, 203-242) work as they are.
+`uninstall()` restores the original forward.
+"""
+from __future__ import annotations
+
+from .attention import moment_forward
+
+_saved: dict = {}
+
+
+def _default_cls():
+    from prime_moment_attention.attention import PrimeMomentAttention  # the reference package
+    return PrimeMomentAttention
+
+
+def install(cls=None):
+    """Patch `cls.forward` (default: the reference PrimeMomentAttention).  Idempotent."""
+    from . import _lib
+    _lib.load()  # fail now, not at the first forward, if the library is missing
+    cls = cls or _default_cls()
+    if cls not in _saved:
+        _saved[cls] = cls.__dict__["forward"]
+        cls.forward = moment_forward
+    return cls
+
+
+def uninstall(cls=None):
+    """Restore the forward saved by install(); a no-op if it was not installed."""
+    cls = cls or _default_cls()
+    fwd = _saved.pop(cls, None)
+    if fwd is not None:
+        cls.forward = fwd
+    return cls
+
+
+def installed(cls=None) -> bool:
+    cls = cls or _default_cls()
+    return cls in _saved

@@ -1,0 +1,98 @@
+"""Host-side logic that needs no GPU: the install() shim, decay tables, argument
+checks and the cache API."""
+import math
+
+import pytest
+import torch
+import torch.nn as nn
+
+import prime_moment_attention_b200 as pma
+from prime_moment_attention_b200 import ops
+
+
+class StandIn(nn.Module):
+    """Has the attributes the reference PrimeMomentAttention defines (attention.py:56-75)."""
+
+    def __init__(self):
+        super().__init__()
+        self.num_heads, self.head_dim, self.num_kv_heads, self.num_kv_groups = 2, 16, 2, 1
+        self.decay, self.eps, self.scaling, self.use_qk_norm = 0.99, 1.0, 0.25, False
+        self.q_proj = self.k_proj = self.v_proj = self.o_proj = nn.Identity()
+
+    def forward(self, hidden_states, state=None, return_state=False):
+        return "original", None
+
+
+def test_install_uninstall_roundtrip():
+    orig = StandIn.__dict__["forward"]
+    pma.install(StandIn)
+    assert pma.installed(StandIn)
+    assert StandIn.forward is pma.moment_forward
+    pma.install(StandIn)  # idempotent
+    pma.uninstall(StandIn)
+    assert StandIn.__dict__["forward"] is orig
+    assert StandIn()(torch.zeros(1, 1, 32))[0] == "original"
+    pma.uninstall(StandIn)  # no-op
+
+
+def test_installed_forward_refuses_cpu_tensors():
+    pma.install(StandIn)
+    try:
+        with torch.no_grad(), pytest.raises(RuntimeError, match="CUDA"):
+            StandIn()(torch.zeros(1, 4, 32))
+    finally:
+        pma.uninstall(StandIn)
+
+
+def test_installed_forward_refuses_autograd():
+    m = pma.PrimeMomentAttention(32, 2, 16)
+    with pytest.raises(RuntimeError, match="inference-only"):
+        m(torch.zeros(1, 4, 32))
+
+
+def test_lambda_tables():
+    t, s = ops.lambda_tensor(0.9, 3, 4, "cpu")
+    assert s == 0 and t.shape == (4,) and torch.allclose(t, torch.full((4,), 0.9))
+    t, s = ops.lambda_tensor([0.1, 0.2, 0.3, 0.4], 3, 4, "cpu")
+    assert s == 0 and t.shape == (4,)
+    t, s = ops.lambda_tensor(torch.rand(3, 4), 3, 4, "cpu")
+    assert s == 4 and t.shape == (12,)
+    with pytest.raises(ValueError):
+        ops.lambda_tensor(torch.rand(5), 3, 4, "cpu")
+
+
+def test_core_rejects_cpu_and_bad_chunk():
+    q = torch.zeros(1, 2, 8, 16)
+    with pytest.raises(ValueError):
+        pma.chunked_prime_ssd_core(q, q, q, chunk_size=0)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pma.chunked_prime_ssd_core(q, q, q)
+
+
+def test_module_constructor_matches_reference_fields():
+    m = pma.PrimeMomentAttention(hidden_size=128, num_heads=4, head_dim=32, num_kv_heads=2, decay=0.999,
+                                 use_qk_norm=True)
+    assert m.num_kv_groups == 2 and m.scaling == 1 / math.sqrt(32) and m.eps == 1.0
+    assert m.chunk_size == 64 and m.chunk_threshold == 512
+    assert m.k_proj.weight.shape == (64, 128)
+    m2 = pma.PrimeMomentAttention(64, 2, 32, decay=[0.9, 0.99])
+    assert torch.allclose(m2.decay_per_head, torch.tensor([0.9, 0.99]))
+    with pytest.raises(ValueError):
+        pma.PrimeMomentAttention(64, 2, 32, decay=[0.9, 0.99, 0.5])
+
+
+def test_cache_api_matches_reference():
+    """Mirrors tests/test_cache.py of the reference."""
+    cache = pma.PrimeMomentCache()
+    assert cache.get_state(0) is None
+    B, H, D = 2, 4, 32
+    st = (torch.randn(B, H, D), torch.randn(B, H, D, D), torch.randn(B, H, D, D), torch.randn(B, H, 1),
+          torch.randn(B, H, D), torch.randn(B, H, D))
+    cache.set_state(layer_idx=0, state=st)
+    got = cache.get_state(layer_idx=0)
+    assert len(got) == 6 and torch.equal(got[0], st[0])
+    cache.update(torch.zeros(B, H, 5, D), torch.zeros(B, H, 5, D), 0)
+    cache.update(torch.zeros(B, H, 5, D), torch.zeros(B, H, 5, D), 1)
+    assert cache.get_seq_length() == 5
+    cache.reset()
+    assert cache.get_state(0) is None and cache.get_seq_length() == 0
