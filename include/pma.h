@@ -94,6 +94,11 @@ PMA_API int pma_version(void);
 /* Static text for a status code. */
 PMA_API const char *pma_status_string(int status);
 
+/* When an entry point returned PMA_ERR_CUDA: the cudaError_t behind it (most
+ * recent such failure on the calling thread; 0 if none) and its text. */
+PMA_API int pma_last_cuda_error(void);
+PMA_API const char *pma_cuda_error_string(int cuda_error);
+
 /* Floats in one head-state: 2*D*D + 3*D + 1 (c/prime_moment.h:17 states the
  * same count for the reference's C runtime). */
 PMA_API size_t pma_state_floats(int D);

@@ -61,8 +61,10 @@ def zero_state(B: int, H: int, D: int):
 
 
 def _lam_table(lam, B: int, H: int):
+    if np.ndim(lam) == 0 and not hasattr(lam, "detach"):
+        return np.full((H,), float(lam)), 0
     lam = _f64(lam)
-    if lam.ndim == 0:
+    if lam.ndim == 0 or lam.size == 1:
         return np.full((H,), float(lam)), 0
     if lam.shape == (H,):
         return lam, 0

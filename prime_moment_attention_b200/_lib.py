@@ -44,7 +44,11 @@ _lib = None
 class PmaError(RuntimeError):
     def __init__(self, fn: str, status: int):
         self.status = status
-        super().__init__(f"{fn} failed: {STATUS.get(status, status)} ({status_string(status)})")
+        msg = f"{fn} failed: {STATUS.get(status, status)} ({status_string(status)})"
+        if status == 6:
+            ce = load().pma_last_cuda_error()
+            msg += f": cudaError {ce} {load().pma_cuda_error_string(ce).decode()}"
+        super().__init__(msg)
 
 
 def load() -> ctypes.CDLL:
@@ -59,6 +63,9 @@ def load() -> ctypes.CDLL:
     L.pma_version.restype = ctypes.c_int
     L.pma_status_string.argtypes = [ctypes.c_int]
     L.pma_status_string.restype = ctypes.c_char_p
+    L.pma_last_cuda_error.restype = ctypes.c_int
+    L.pma_cuda_error_string.argtypes = [ctypes.c_int]
+    L.pma_cuda_error_string.restype = ctypes.c_char_p
     L.pma_state_floats.argtypes = [ctypes.c_int]
     L.pma_state_floats.restype = ctypes.c_size_t
     L.pma_supported_head_dims.argtypes = [ctypes.c_int, _P(ctypes.c_int), ctypes.c_int]

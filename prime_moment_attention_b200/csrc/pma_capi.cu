@@ -14,6 +14,14 @@ struct DevInfo {
     bool valid = false;
 };
 
+thread_local int g_last_cuda_error = 0;
+
+// PMA_ERR_CUDA with the cause remembered for pma_last_cuda_error().
+int cuda_fail(cudaError_t e) {
+    g_last_cuda_error = (int)e;
+    return PMA_ERR_CUDA;
+}
+
 inline int d_ok(const DevInfo &d) { return d.major == 10 ? PMA_OK : PMA_ERR_DEVICE; }
 
 constexpr int kMaxDevices = 64;
@@ -22,12 +30,16 @@ std::mutex g_dev_mu;
 
 int device_info(DevInfo *out) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return PMA_ERR_CUDA;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) return cuda_fail(ce);
+    if (dev < 0 || dev >= kMaxDevices) return PMA_ERR_DEVICE;
     std::lock_guard<std::mutex> lk(g_dev_mu);
     if (!g_dev[dev].valid) {
         DevInfo d;
-        if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return PMA_ERR_CUDA;
-        if (cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return PMA_ERR_CUDA;
+        if ((ce = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+            return cuda_fail(ce);
+        if ((ce = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+            return cuda_fail(ce);
         d.valid = true;
         g_dev[dev] = d;
     }
@@ -40,8 +52,9 @@ bool supported_dtype(int t) { return t == PMA_F32 || t == PMA_BF16; }
 size_t esize(int t) { return t == PMA_F32 ? 4 : 2; }
 
 // Each row of D elements must start on a 16-byte boundary (vector loads, TMA).
-int check_seq(const pma_seq_tensor *t, bool use_l) {
-    if (!t || !t->data) return PMA_ERR_ARGUMENT;
+int check_seq(const pma_seq_tensor *t, bool use_l, bool empty = false) {
+    if (!t) return PMA_ERR_ARGUMENT;
+    if (!t->data) return empty ? (supported_dtype(t->dtype) ? PMA_OK : PMA_ERR_DTYPE) : PMA_ERR_ARGUMENT;
     if (!supported_dtype(t->dtype)) return PMA_ERR_DTYPE;
     const int64_t step = 16 / (int64_t)esize(t->dtype);
     if (reinterpret_cast<uintptr_t>(t->data) % 16) return PMA_ERR_LAYOUT;
@@ -90,19 +103,21 @@ Plan make_plan(int B, int H, int L, int D, int dtype, int sms) {
     Plan p;
     p.tc = tc_supported(D, dtype);
     p.chunk = p.tc ? TC_CHUNK : simt_chunk(D);
-    const int BH = B * H;
+    const long BH = (long)B * H;
     const int nchunks = (L + p.chunk - 1) / p.chunk;
-    // CTAs resident per SM: SIMT D<=64 fits two, D=128 and the tensor-core kernel one.
-    const int per_sm = (!p.tc && D <= 64) ? 2 : 1;
-    const long target = (long)sms * per_sm;
+    // CTAs resident per SM: SIMT D<=64 fits two; D=128 and the tensor-core kernel one.
+    const long slots = (long)sms * ((!p.tc && D <= 64) ? 2 : 1);
+    // Split sequences into segments only when B*H leaves SMs idle, and only into as
+    // many as fit one wave (a partial second wave costs more than the idle SMs).
     int nseg = 1;
-    if (BH > 0 && BH < target) nseg = (int)((target + BH - 1) / BH);
+    if (BH > 0 && BH * 2 <= slots) nseg = (int)(slots / BH);
     if (nseg > nchunks) nseg = nchunks;
     if (nseg < 1) nseg = 1;
     const int seg_chunks = (nchunks + nseg - 1) / nseg;
     p.nseg = seg_chunks > 0 ? (nchunks + seg_chunks - 1) / seg_chunks : 1;
     p.seg_len = seg_chunks * p.chunk;
-    if (p.nseg > 1) p.ws_bytes = (size_t)BH * p.nseg * state_floats(D) * sizeof(float);
+    p.ws_bytes = p.tc ? WS_HEADER : 0;
+    if (p.nseg > 1) p.ws_bytes = WS_HEADER + (size_t)BH * p.nseg * slot_floats(D) * sizeof(float);
     return p;
 }
 
@@ -131,6 +146,10 @@ const char *pma_status_string(int status) {
     }
 }
 
+int pma_last_cuda_error(void) { return g_last_cuda_error; }
+
+const char *pma_cuda_error_string(int cuda_error) { return cudaGetErrorString((cudaError_t)cuda_error); }
+
 size_t pma_state_floats(int D) { return D > 0 ? state_floats(D) : 0; }
 
 int pma_supported_head_dims(int dtype, int *dims, int cap) {
@@ -155,9 +174,11 @@ int pma_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_s
     if (B < 0 || H <= 0 || L < 0 || !lambda || lambda_stride_b < 0) return PMA_ERR_ARGUMENT;
     if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
     int rc;
-    if ((rc = check_seq(q, true)) || (rc = check_seq(k, true)) || (rc = check_seq(v, true))) return rc;
+    const bool empty = (L == 0 || B == 0);  // no element is touched: null data is fine
+    if ((rc = check_seq(q, true, empty)) || (rc = check_seq(k, true, empty)) || (rc = check_seq(v, true, empty)))
+        return rc;
     if (q->dtype != k->dtype || q->dtype != v->dtype) return PMA_ERR_DTYPE;
-    if (y && (rc = check_seq(y, true))) return rc;
+    if (y && (rc = check_seq(y, true, empty))) return rc;
     if (state_in && (rc = check_state(state_in))) return rc;
     if (state_out && (rc = check_state(state_out))) return rc;
     DevInfo di;
@@ -179,7 +200,7 @@ int pma_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_s
                                                         : cudaMemcpyAsync(dst[i], src[i], n[i] * 4,
                                                                           cudaMemcpyDeviceToDevice, st))
                                    : cudaMemsetAsync(dst[i], 0, n[i] * 4, st);
-            if (e != cudaSuccess) return PMA_ERR_CUDA;
+            if (e != cudaSuccess) return cuda_fail(e);
         }
         return PMA_OK;
     }
@@ -202,17 +223,22 @@ int pma_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_s
     p.lambda = lambda;
     p.lam_sb = lambda_stride_b;
     p.eps = eps;
+    p.status = nullptr;
 
     cudaError_t e;
+    if (pl.ws_bytes) {  // clear the status word the tensor-core kernel reports timeouts in
+        p.status = reinterpret_cast<int *>(workspace);
+        if ((e = cudaMemsetAsync(p.status, 0, sizeof(int), st)) != cudaSuccess) return cuda_fail(e);
+    }
     if (pl.nseg == 1) {
         p.in = user_ref(state_in);
         p.out = user_ref(state_out);
         p.state_only = 0;
         e = launch_prefill(pl, p, D, q->dtype, ydt, dim3(BH, 1), st);
-        return e == cudaSuccess ? PMA_OK : PMA_ERR_CUDA;
+        return e == cudaSuccess ? PMA_OK : cuda_fail(e);
     }
 
-    float *ws = reinterpret_cast<float *>(workspace);
+    float *ws = reinterpret_cast<float *>(reinterpret_cast<char *>(workspace) + WS_HEADER);
     // 1. each segment's own state from zero (the last one only when no y is wanted)
     PrefillParams ps = p;
     ps.y = SeqOut{nullptr, 0, 0, 0};
@@ -221,18 +247,18 @@ int pma_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_s
     ps.state_only = 1;
     const int nstate = y ? pl.nseg - 1 : pl.nseg;
     e = launch_prefill(pl, ps, D, q->dtype, ydt, dim3(BH, nstate), st);
-    if (e != cudaSuccess) return PMA_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_fail(e);
     // 2. in-place prefix: state entering every segment (and the final state if no y)
     e = launch_segment_prefix(BH, H, D, pl.nseg, pl.seg_len, L, ws, user_ref(state_in),
                               y ? user_ref(nullptr) : user_ref(state_out), lambda, lambda_stride_b, st);
-    if (e != cudaSuccess) return PMA_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_fail(e);
     if (!y) return PMA_OK;
     // 3. full pass, every segment starting from its carried state
     p.in = packed_ref(ws, pl.nseg);
     p.out = user_ref(state_out);
     p.state_only = 0;
     e = launch_prefill(pl, p, D, q->dtype, ydt, dim3(BH, pl.nseg), st);
-    return e == cudaSuccess ? PMA_OK : PMA_ERR_CUDA;
+    return e == cudaSuccess ? PMA_OK : cuda_fail(e);
 }
 
 int pma_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
@@ -241,8 +267,9 @@ int pma_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_
     if (N < 0 || H <= 0 || !lambda || lambda_stride_n < 0) return PMA_ERR_ARGUMENT;
     if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
     int rc;
-    if ((rc = check_seq(q, false)) || (rc = check_seq(k, false)) || (rc = check_seq(v, false)) ||
-        (rc = check_seq(y, false)))
+    const bool empty = N == 0;
+    if ((rc = check_seq(q, false, empty)) || (rc = check_seq(k, false, empty)) || (rc = check_seq(v, false, empty)) ||
+        (rc = check_seq(y, false, empty)))
         return rc;
     if (q->dtype != k->dtype || q->dtype != v->dtype) return PMA_ERR_DTYPE;
     if ((rc = check_state(state_in)) || (rc = check_state(state_out))) return rc;
@@ -263,7 +290,7 @@ int pma_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_
     p.out = *state_out;
     p.eps = eps;
     cudaError_t e = launch_decode(p, D, q->dtype, y->dtype, reinterpret_cast<cudaStream_t>(stream));
-    return e == cudaSuccess ? PMA_OK : PMA_ERR_CUDA;
+    return e == cudaSuccess ? PMA_OK : cuda_fail(e);
 }
 
 int pma_state_combine(int B, int H, int D, const float *lambda, int64_t lambda_stride_b, int64_t len,
@@ -277,7 +304,7 @@ int pma_state_combine(int B, int H, int D, const float *lambda, int64_t lambda_s
     if (B == 0) return PMA_OK;
     cudaError_t e = launch_state_combine(B, H, D, lambda, lambda_stride_b, len, *T, *P,
                                          reinterpret_cast<cudaStream_t>(stream));
-    return e == cudaSuccess ? PMA_OK : PMA_ERR_CUDA;
+    return e == cudaSuccess ? PMA_OK : cuda_fail(e);
 }
 
 }  // extern "C"

@@ -66,8 +66,13 @@ struct HeadPtrs {
     float *S0, *S1, *S2, *Z0, *Z1, *Z2;
 };
 
+__host__ __device__ constexpr size_t state_floats(int D) { return 2 * (size_t)D * D + 3 * (size_t)D + 1; }
+// Slot stride of the packed scratch layout: state_floats rounded up to 32 floats,
+// so every slot (and every S1/S2 row in it) starts on a 128-byte boundary.
+__host__ __device__ constexpr size_t slot_floats(int D) { return (state_floats(D) + 31) / 32 * 32; }
+
 // Either the user's six-array state (index bh) or a packed scratch layout
-// [bh][slot][F] with F = 2D^2 + 3D + 1 ordered S1 | S2 | S0 | Z1 | Z2 | Z0.
+// [bh][slot][slot_floats(D)] ordered S1 | S2 | S0 | Z1 | Z2 | Z0.
 struct StateRef {
     pma_state user;      // used when packed == nullptr and user.S1 != nullptr
     float *packed;
@@ -76,8 +81,7 @@ struct StateRef {
     __device__ __forceinline__ HeadPtrs at(int bh, int slot, int D) const {
         HeadPtrs r;
         if (packed) {
-            const size_t F = 2 * (size_t)D * D + 3 * (size_t)D + 1;
-            float *b = packed + ((size_t)bh * slots + slot) * F;
+            float *b = packed + ((size_t)bh * slots + slot) * slot_floats(D);
             r.S1 = b;
             r.S2 = b + (size_t)D * D;
             r.S0 = b + 2 * (size_t)D * D;
@@ -96,6 +100,5 @@ struct StateRef {
     }
 };
 
-__host__ __device__ constexpr size_t state_floats(int D) { return 2 * (size_t)D * D + 3 * (size_t)D + 1; }
 
 }  // namespace pma

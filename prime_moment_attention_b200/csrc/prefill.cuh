@@ -19,7 +19,11 @@ struct PrefillParams {
     StateRef out;         // user: final state (last segment only); packed: slot = segment
     float eps;
     int state_only;       // 1: skip the readout, start every segment from zero, write its state to `out`
+    int *status;          // device status word (0 = ok); bounded waits record a code here
 };
+
+// Workspace layout: [header: 256 B, int status word first][per-segment states, float32].
+constexpr size_t WS_HEADER = 256;
 
 struct DecodeParams {
     int N, H;

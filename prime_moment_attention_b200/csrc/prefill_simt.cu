@@ -301,12 +301,13 @@ __global__ void segment_prefix_kernel(int BH, int H, int D, int nseg, int seg_le
         return hp.Z0;
     };
     float P = in.present() ? *comp(in.at(bh, 0, D)) : 0.f;
-    float *base = ws + (size_t)bh * nseg * F + f;
+    const size_t FS = slot_floats(D);
+    float *base = ws + (size_t)bh * nseg * FS + f;
     const int nprefix = final_out.present() ? nseg : nseg - 1;
     for (int sg = 0; sg < nseg; ++sg) {
         float T = 0.f;
-        if (sg < nprefix) T = base[(size_t)sg * F];
-        base[(size_t)sg * F] = P;
+        if (sg < nprefix) T = base[(size_t)sg * FS];
+        base[(size_t)sg * FS] = P;
         if (sg < nprefix) {
             const int len = min(seg_len, L - sg * seg_len);
             P = fmaf((float)pow(lam, (double)len), P, T);

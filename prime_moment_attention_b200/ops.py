@@ -107,12 +107,13 @@ def _stream(device) -> int:
 def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
             state: Optional[StateTuple] = None, eps: float = 1.0, return_state: bool = True,
             out_dtype: Optional[torch.dtype] = None, y_out: Optional[torch.Tensor] = None,
-            want_y: bool = True):
+            want_y: bool = True, check: bool = False):
     """Chunked prefill over q, k, v [B,H,L,D] (q pre-scaled by 1/sqrt(D)).
 
     Returns (y [B,H,L,D] or None, final state or None).  `y_out` may be a
     preallocated [B,H,L,D] view with any strides (e.g. a transpose of [B,L,H,D]).
-    `want_y=False` runs the state-only pass."""
+    `want_y=False` runs the state-only pass.  `check=True` synchronises and raises
+    if the kernel recorded a failure in its status word (a bounded wait expired)."""
     dev = _require_cuda(q, k, v)
     if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
         raise ValueError(f"q, k, v must share one [B,H,L,D] shape; got {tuple(q.shape)}, {tuple(k.shape)}, "
@@ -148,6 +149,10 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
                         st_in, st_out, float(eps), ys, ws.data_ptr() if ws is not None else None, ws_bytes,
                         _stream(dev))
     _lib.check("pma_prefill", rc)
+    if check and ws is not None:
+        code = int(ws[:4].view(torch.int32).item())
+        if code != 0:
+            raise RuntimeError(f"pma_prefill: kernel status word {code} (a bounded wait expired)")
     return y, st_out_t
 
 

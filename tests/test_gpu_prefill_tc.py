@@ -1,0 +1,97 @@
+"""Tensor-core (tcgen05) prefill: bf16 inputs, D = 64, against the float64 oracle.
+
+Bar: 2e-2 max relative error on y and on each final-state component (bf16
+operands, float32 accumulation and state).  Each call also checks the kernel's
+status word (no bounded wait expired)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from prime_moment_attention_b200 import _lib, ops, synth
+from tests.helpers import TOL_BF16, TOL_F32, assert_close, assert_state_close, cpu64, lam_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(B, H, L, seed, lam=None, state=None, out_dtype=torch.float32):
+    D = 64
+    q, k, v = synth.make_qkv(B, H, L, D, seed=seed, dtype=torch.bfloat16, device="cuda")
+    if lam is None:
+        lam = synth.make_lambdas(H, 0.99, 0.9999, seed=seed)
+    y, st = ops.prefill(q, k, v, lam, state=state, out_dtype=out_dtype, check=True)
+    lam_ref = lam.double().numpy() if torch.is_tensor(lam) else lam
+    y_ref, st_ref = O.prefill(q, k, v, lam_ref, state=None if state is None else tuple(s.cpu() for s in state))
+    return y, st, y_ref, st_ref
+
+
+@pytest.mark.parametrize("L", [1, 5, 127, 128, 129, 300, 1000])
+def test_tc_lengths(L):
+    y, st, y_ref, st_ref = _run(2, 3, L, seed=L)
+    assert_close(y, y_ref, TOL_BF16, "y")
+    assert_state_close(st, st_ref, TOL_BF16)
+
+
+def test_tc_incoming_state_and_bf16_out():
+    B, H = 2, 4
+    lam = torch.rand(B, H) * 0.02 + 0.98
+    st0 = synth.make_state(B, H, 64, lam[0], seed=3, t0=300, sigma=0.05, device="cuda")
+    y, st, y_ref, st_ref = _run(B, H, 517, seed=4, lam=lam, state=st0, out_dtype=torch.bfloat16)
+    assert_close(y, y_ref, TOL_BF16, "y")
+    assert_state_close(st, st_ref, TOL_BF16)
+
+
+def test_tc_small_decay():
+    """Decays far from 1 (l^127 underflows toward zero): masks and weights stay finite."""
+    lam = torch.tensor([0.5, 0.1, 0.9])
+    y, st, y_ref, st_ref = _run(1, 3, 260, seed=7, lam=lam)
+    assert_close(y, y_ref, TOL_BF16, "y")
+    assert_state_close(st, st_ref, TOL_BF16)
+
+
+def test_tc_segmented():
+    """B*H well below the SM count: sequences split into segments (state-only pass,
+    prefix, full pass), all on the tensor-core kernel."""
+    B, H, L = 1, 4, 4096 + 77
+    assert _lib.load().pma_prefill_workspace_bytes(B, H, L, 64, _lib.PMA_BF16) > 256
+    lam = torch.tensor([0.999, 0.99, 0.9999, 0.95])
+    st0 = synth.make_state(B, H, 64, lam, seed=8, t0=1000, sigma=0.02, device="cuda")
+    y, st, y_ref, st_ref = _run(B, H, L, seed=9, lam=lam, state=st0)
+    assert_close(y, y_ref, TOL_BF16, "y")
+    assert_state_close(st, st_ref, TOL_BF16)
+    q, k, v = synth.make_qkv(B, H, L, 64, seed=9, dtype=torch.bfloat16, device="cuda")
+    _, st_only = ops.prefill(q, k, v, lam, state=st0, want_y=False, check=True)
+    assert_state_close(st_only, st_ref, TOL_BF16, "state-only")
+
+
+def test_tc_strided_module_layout():
+    """q/k/v as views of [B,L,H,D] projections, y into a [B,L,H,D] buffer."""
+    B, H, L, D = 2, 3, 300, 64
+    base = torch.nn.functional.normalize(torch.randn(B, L, 3 * H, D, device="cuda"), dim=-1).to(torch.bfloat16)
+    q, k, v = (base[:, :, i * H:(i + 1) * H].transpose(1, 2) for i in range(3))
+    q = (q.float() * 0.125).to(torch.bfloat16)
+    y_bl = torch.empty(B, L, H, D, device="cuda", dtype=torch.bfloat16)
+    _, st = ops.prefill(q, k, v, 0.995, y_out=y_bl.transpose(1, 2), check=True)
+    y_ref, st_ref = O.prefill(q, k, v, 0.995)
+    assert_close(y_bl.transpose(1, 2), y_ref, TOL_BF16, "y")
+    assert_state_close(st, st_ref, TOL_BF16)
+
+
+def test_tc_config2_full_size():
+    """Config 2 at full size (B=8, H=12, L=8192): two head-states against the oracle
+    over all 8192 tokens, and every head-state against the float32 CUDA-core kernel
+    run on the same (bf16-valued) inputs."""
+    c = synth.CONFIG2
+    B, H, L, D = c["B"], c["H"], c["L"], c["D"]
+    q, k, v = synth.make_qkv(B, H, L, D, seed=c["seed"], dtype=torch.bfloat16, device="cuda")
+    lam = synth.make_lambdas(H, *c["lam"], seed=c["seed"])
+    y, st = ops.prefill(q, k, v, lam, out_dtype=torch.float32, check=True)
+    for (bb, hh) in [(0, 0), (5, 11)]:
+        y_ref, st_ref = O.prefill(q[bb:bb + 1, hh:hh + 1], k[bb:bb + 1, hh:hh + 1], v[bb:bb + 1, hh:hh + 1],
+                                  lam_np(lam)[hh:hh + 1])
+        assert_close(y[bb:bb + 1, hh:hh + 1], y_ref, TOL_BF16, f"y[{bb},{hh}]")
+        assert_state_close(tuple(s[bb:bb + 1, hh:hh + 1] for s in st), st_ref, TOL_BF16, f"state[{bb},{hh}]")
+    y32, st32 = ops.prefill(q.float(), k.float(), v.float(), lam, out_dtype=torch.float32)
+    assert_close(y, cpu64(y32), TOL_BF16, "y vs fp32 kernel")
+    for a, b_ in zip(st, st32):
+        assert_close(a, cpu64(b_), TOL_BF16, "state vs fp32 kernel")
