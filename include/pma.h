@@ -146,6 +146,28 @@ PMA_API int pma_prefill(int B, int H, int L, int D,
                 void *workspace, size_t workspace_bytes, pma_stream_t stream);
 
 /*
+ * pma_prefill without a caller-provided workspace, for callers that cannot
+ * allocate device memory (a plugin whose host application owns all device memory
+ * through its own pool, FFI callers without a device allocator, loops where an
+ * allocation would synchronise the device).  No counterpart in the reference:
+ * the reference always allocates through ATen.
+ *
+ * Same arguments and results as pma_prefill.  Its scratch is a 16 MiB buffer
+ * compiled into the library (one per GPU that loads it, held until exit);
+ * problems whose plan needs more (pma_prefill_workspace_bytes > 16 MiB: float32
+ * or D = 128 with few head-states and long sequences) return PMA_ERR_WORKSPACE.
+ * The first call on a device looks up the buffer's device address; make it
+ * before any stream capture.  All calls on a device share the buffer: calls that
+ * overlap on the GPU race and must be serialised by the caller.  Allocates
+ * nothing.
+ */
+PMA_API int pma_prefill_no_alloc(int B, int H, int L, int D,
+                                 const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                                 const float *lambda, int64_t lambda_stride_b,
+                                 const pma_state *state_in, const pma_state *state_out,
+                                 float eps, const pma_seq_tensor *y, pma_stream_t stream);
+
+/*
  * One recurrent decode step for N x H head-states (N = batch rows, or
  * sequences x layers when all layers' heads are batched in one launch).
  *
