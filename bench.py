@@ -225,27 +225,23 @@ def time_steps(fn, steps, warmup, ws, device, stream):
     return e0.elapsed_time(e1) / steps  # ms per step
 
 
-def run_ours(args):
+def bench_prefill(args, ws, rank, device, stream, peaks):
+    """Config-2 prefill: device-timed throughput, roofline, and the e2e call from host buffers."""
     import torch
-    ws, rank, local = dist_setup()
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
     from prime_moment_attention_b200 import _lib, ops, synth
-
-    hbm_peak, tc_peak, peak_kind = _peaks()
-    stream = torch.cuda.current_stream(device)
+    hbm_peak, tc_peak, peak_kind = peaks
     c = PREFILL
     B, H, L, D = c["B"], c["H"], c["L"], c["D"]
     q, k, v = synth.make_qkv(B, H, L, D, seed=c["seed"] + 1000 * rank, dtype=torch.bfloat16, device=device)
     lam = synth.make_lambdas(H, *c["lam"], seed=c["seed"]).to(device)
     y = torch.empty_like(q)
     ws_bytes = _lib.load().pma_prefill_workspace_bytes(B, H, L, D, _lib.PMA_BF16)
-    launches_per_step = 3 if ws_bytes else 1
+    launches_per_step = 3 if ws_bytes > 256 else 1
 
     def step():
         ops.prefill(q, k, v, lam, y_out=y, return_state=True)
 
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(device.index)
     for _ in range(args.warmup):
         step()
     clocks.start()
@@ -253,7 +249,6 @@ def run_ours(args):
     clk = clocks.stop()
     ms = max_over_ranks(ms, ws, device)
     tokens = B * L * ws
-    value = tokens / (ms * 1e-3)
     tokheads = B * L * H
     algo_bytes = tokheads * PREFILL_BYTES_PER_TOKHEAD
     algo_flop = tokheads * PREFILL_FLOP_PER_TOKHEAD
@@ -265,7 +260,7 @@ def run_ours(args):
             "timed": "whole pma_prefill call (all its launches), CUDA events on the launching stream",
             "algorithmic_bytes_per_launch": algo_bytes, "algorithmic_flop_per_launch": algo_flop}
 
-    # ---- e2e through the public API with host buffers
+    # e2e through the public API with host buffers
     e2e_steps = max(1, min(args.steps, 5))
     qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
     yh = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
@@ -281,9 +276,24 @@ def run_ours(args):
     e2e_ms = max_over_ranks(time_steps(e2e_step, e2e_steps, 1, ws, device, stream), ws, device)
     h2d = 3 * q.numel() * q.element_size()
     d2h = y.numel() * y.element_size()
-    del qh, kh, vh, yh, qd, kd, vd
+    return {"metric": "prefill_tok_per_s", "value": round(tokens / (ms * 1e-3), 1), "unit": "tok/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": B * ws, "seq_len": L,
+                       "parallelism": f"dp{ws} (batch x head shards, no collective)",
+                       "l2": "inputs 403 MB per GPU > 126 MB L2; no flush"},
+            "roofline": roof,
+            "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
+                    "path": "pinned host q,k,v -> H2D -> ops.prefill (C ABI pma_prefill) -> D2H y"},
+            "gpu_launches": args.steps * launches_per_step, "clocks": clk}
 
-    # ---- decode (config 3)
+
+def bench_decode(args, ws, rank, device, stream, peaks):
+    """Config-3 decode step: all layers' heads of 256 sequences in one launch, in place."""
+    import torch
+    from prime_moment_attention_b200 import ops, synth
+    hbm_peak, _, peak_kind = peaks
     dc = DECODE
     N, HD = dc["seqs"], dc["layers"] * dc["H"]
     lam_d = synth.make_lambdas(HD, *dc["lam"], seed=dc["seed"]).to(device)
@@ -298,7 +308,7 @@ def run_ours(args):
         it[0] += 1
         ops.decode_step(qq, kk, vv, lam_d, st, inplace=True, y_out=yd)
 
-    dclk = ClockSampler(local)
+    dclk = ClockSampler(device.index)
     for _ in range(max(3, args.warmup)):
         dstep()
     dclk.start()
@@ -306,34 +316,41 @@ def run_ours(args):
     dclk_r = dclk.stop()
     d_bytes = N * HD * DECODE_BYTES_PER_HEADSTEP
     d_bw = d_bytes / (dms * 1e-3) / 1e9
-    decode = {"metric": "decode_step_us", "value": round(dms * 1e3, 2), "unit": "us/step",
-              "higher_is_better": False, "steps": dc["steps"],
-              "config": {"workload": "config3 decode: 256 seqs x 12 layers x 12 heads per GPU, D=64, bf16 q/k/v, "
-                                     "fp32 state in place, all layers' heads in one launch",
-                         "state_bytes": N * HD * (2 * 64 * 64 + 3 * 64 + 1) * 4, "l2": "state 1.24 GB > L2"},
-              "roofline": {"bound": "hbm", "achieved": round(d_bw, 1), "peak": hbm_peak, "unit": "GB/s",
-                           "frac": round(d_bw / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
-                           "algorithmic_bytes_per_launch": d_bytes},
-              "gpu_launches": dc["steps"], "clocks": dclk_r}
-    del st, toks
+    return {"metric": "decode_step_us", "value": round(dms * 1e3, 2), "unit": "us/step",
+            "higher_is_better": False, "steps": dc["steps"],
+            "config": {"workload": "config3 decode: 256 seqs x 12 layers x 12 heads per GPU, D=64, bf16 q/k/v, "
+                                   "fp32 state in place, all layers' heads in one launch",
+                       "state_bytes": N * HD * (2 * 64 * 64 + 3 * 64 + 1) * 4, "l2": "state 1.24 GB > L2"},
+            "roofline": {"bound": "hbm", "achieved": round(d_bw, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(d_bw / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": d_bytes},
+            "gpu_launches": dc["steps"], "clocks": dclk_r}
 
-    line = {"metric": "prefill_tok_per_s", "value": round(value, 1), "unit": "tok/s", "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": B * ws, "seq_len": L,
-                       "parallelism": f"dp{ws} (batch x head shards, no collective)",
-                       "l2": "inputs 403 MB per GPU > 126 MB L2; no flush"},
-            "roofline": roof,
-            "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
-                    "path": "pinned host q,k,v -> H2D -> ops.prefill (C ABI pma_prefill) -> D2H y"},
-            "gpu_launches": args.steps * launches_per_step,
-            "clocks": clk,
-            "decode": decode}
+
+def run_ours(args):
+    import torch
+    ws, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream(device)
+    peaks = _peaks()
+    line = {}
+    if args.workload in ("both", "prefill"):
+        line = bench_prefill(args, ws, rank, device, stream, peaks)
+        torch.cuda.empty_cache()
+    if args.workload in ("both", "decode"):
+        dec = bench_decode(args, ws, rank, device, stream, peaks)
+        if line:
+            line["decode"] = dec
+        else:
+            line = dict(dec, n_gpus=ws, warmup=args.warmup, scaling="weak", dtype="bf16", data="synthetic",
+                        vs_baseline=None)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and ref_bench_path():
         try:
-            line["cpu_baseline"] = cpu_prefill_sample()
-            line["decode"]["cpu_baseline"] = cpu_decode_sample()
+            if "decode" in line:
+                line["decode"]["cpu_baseline"] = cpu_decode_sample()
+            if line.get("metric") == "prefill_tok_per_s":
+                line["cpu_baseline"] = cpu_prefill_sample()
         except Exception as e:  # the baseline must not sink the GPU number
             line["cpu_baseline"] = {"error": str(e)[:200]}
     if rank == 0:
@@ -351,6 +368,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["both", "prefill", "decode"], default="both",
+                    help="profiling aid: run only one part (the JSON line then lacks the other)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
