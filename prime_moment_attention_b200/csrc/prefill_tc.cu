@@ -1,77 +1,84 @@
 // prefill_tc.cu -- chunked prefill on tcgen05 tensor cores (bf16 inputs, D = 64).
 //
 // Same recurrence as chunked_prime_ssd_core (src/prime_moment_attention/chunked_ssd.py:48-184),
-// evaluated per 128-token chunk with the moment features written as GEMMs:
-//   psi(q) = [q | q^2/2],  phi(k) = [k | k^2]           (2D = 128 features)
-//   A      = psi(Q) phi(K)^T                  M=128 tokens, N=128 tokens, K=128 features
-//   P[i,j] = l^(i-j) (1 + A[i,j]),  j <= i    (decay mask, chunked_ssd.py:79-92)
-//   num    = P V                              M=128, N=64,  K=128 tokens   (:93)
-//   carry  = psi(Q) [S1; S2]                  M=128, N=64,  K=128 features (:139-148)
-//   dS     = phi(K)^T (w . V), w_j = l^(n-1-j) M=128 features, N=64, K=128 tokens (:96-107)
-//   y_i    = (num_i + l^(i+1) (S0 + carry_i)) / max(den_i + l^(i+1) (Z0 + psi(q_i).[Z1;Z2]), eps)
-//   S      = l^n S + dS (float32, carried in registers of the state warpgroup)
-// Operands are bf16 in shared memory (TMA tiles with the 128-byte swizzle, or
-// tiles written by the kernel with the same swizzle); accumulators are float32
-// in tensor memory.  The running state stays float32; a bf16 copy of it is the
-// B operand of the carry GEMM.
+// evaluated per 128-token chunk (n <= 128 valid tokens) with the moment features
+// psi(q) = [q | q^2/2], phi(k) = [k | k^2] (128 features) written as GEMMs on
+// rescaled operands, so that almost all of the arithmetic runs on tensor cores:
 //
-// Warp roles (384 threads, one CTA per SM):
-//   warp 0       TMA producer: q, k, v chunk tiles, two stages
-//   warp 1       MMA issuer (one thread) and tensor-memory owner (512 columns)
-//   warps 4-7    "prep" warpgroup: q^2/2, k^2, w.v tiles and the column sums that
-//                update S0, Z1, Z2; then the decay-mask epilogue that turns A into
-//                bf16 P and the per-token denominators
-//   warps 8-11   "state" warpgroup: state update from dS (thread f owns feature row
-//                f), bf16 state tile for the next carry GEMM, then the output epilogue
-// Every wait on an mbarrier is bounded by the global timer; on expiry the kernel
-// records a status code in the workspace header, every role stops, and the CTA
-// waits for its in-flight copies and GEMMs before freeing tensor memory.
+//   g_i = l^(i+1)   (carry into token i)      w_j = l^(n-1-j)  (token j to chunk end, 0 if j >= n)
+//   Qg  = g . q,  Q2g = g . q^2/2             Vw = w . v                 (rows scaled, bf16)
+//   At  = [Qg | Q2g] [K | K^2]^T  = g_i (q_i.k_j + q_i^2.k_j^2/2)       (M=N=128, K=128)
+//   P'  = l^(i-n+1) + l^-n At     = l^(i-j) (1 + ...) / w_j   for j <= i, else 0
+//   ACC = [Qg | Q2g] [S1; S2]  +  P' Vw   =  g_i carry_i + num_i          (chunked_ssd.py:93,139-148)
+//   DEN = [Qg | Q2g] [Z1; Z2]  +  P' w    =  g_i cden_i  + den_i           (:94,149-153)
+//   y_i = (ACC_i + g_i S0) / max(DEN_i + g_i Z0, eps)                      (:155-157)
+//   dS  = [K | K^2]^T Vw,  dZ = [K | K^2]^T w,  dS0 = Vw^T 1             (:96-111)
+//   S   = l^n S + dS   (float32, in registers of the state warpgroup)     (:162-169)
+// The per-element decay mask of the reference becomes one FMA per element;
+// denominators and the S0/Z1/Z2 updates are N=16 GEMMs against one-row tiles.
+// The rescaling keeps every factor inside float32/bf16 range for l >= 0.55
+// (l^-128 < 1e34, l^128 > 1e-34); head-states with a smaller decay run the
+// float32 CUDA-core chunk loop (prefill_simt_body.cuh) inside this kernel.
+//
+// Data: q/k/v chunk tiles arrive by TMA (4-D tensor maps over the strided
+// tensors, 128-byte swizzle) into two stages; prep overwrites q by Qg and v by
+// Vw in place and writes Q2g and K^2 to double-buffered tiles.  Accumulators
+// live in tensor memory (512 columns): At x2 (P' is written back over the
+// consumed At columns and read by the P'-GEMMs from TMEM), ACC x2, dS, DEN x2,
+// dZ, dS0.  The bf16 state copy [S1; S2] and the one-row [Z1; Z2] tile that feed
+// the carry GEMMs are double-buffered.
+//
+// Warp roles (512 threads, one CTA per SM):
+//   warp 0        TMA producer
+//   warp 1        MMA issuer (one thread, event driven: issues each chunk's GEMM
+//                 groups as soon as their inputs are ready) and TMEM owner
+//   warps 4-7     prep: Qg, Q2g, K^2, Vw for each chunk
+//   warps 8-11    mask: At -> P' in tensor memory
+//   warps 12-15   state and output: S += dS (thread f owns feature row f), bf16
+//                 state tiles for the next chunk, then y for the chunk's 128 tokens
+// Every wait is bounded by the global timer; on expiry the kernel records a status
+// code in the workspace header, every role stops, and the CTA waits for its
+// in-flight copies and GEMMs before freeing tensor memory.
 #include <cuda.h>
 
 #include "prefill.cuh"
+#include "prefill_simt_body.cuh"
 
 namespace pma {
 namespace tc {
 
 constexpr int C = TC_CHUNK;   // tokens per chunk
 constexpr int D = 64;
-constexpr int F = 2 * D;      // moment features
-constexpr int TILE = C * D * 2;          // one [128 x 64] bf16 tile = 16 KiB
-constexpr int STAGE = 3 * TILE;          // q, k, v
-constexpr int OFF_Q2 = 2 * STAGE;        // q^2/2
-constexpr int OFF_K2 = OFF_Q2 + TILE;    // k^2
-constexpr int OFF_VW = OFF_K2 + TILE;    // w . v
-constexpr int OFF_P = OFF_VW + TILE;     // P, two 64-column atoms
-constexpr int OFF_SB = OFF_P + 2 * TILE; // bf16 state [128 features][64 values], two buffers
-constexpr int OFF_SMALL = OFF_SB + 2 * TILE;
+constexpr int TILE = C * D * 2;           // [128 x 64] bf16 = 16 KiB
+constexpr int STAGE = 3 * TILE;           // q (-> Qg), k, v (-> Vw)
+constexpr int OFF_DER = 2 * STAGE;        // per buffer: Q2g, K^2
+constexpr int OFF_SB = OFF_DER + 4 * TILE;    // bf16 [S1; S2], [128 features][64 values], x2
+constexpr int ROW1 = 4096;                // one-row K-major tile: 2 atoms x 16 rows x 128 B
+constexpr int OFF_ZT = OFF_SB + 2 * TILE;     // [Z1; Z2] row, x2
+constexpr int OFF_W16 = OFF_ZT + 2 * ROW1;    // w row: full chunks, last partial chunk
+constexpr int OFF_ONES = OFF_W16 + 2 * ROW1;  // ones row
+constexpr int OFF_SMALL = OFF_ONES + ROW1;
+constexpr float LMIN = 0.55f;             // smallest decay the rescaled operands serve
 
-// Barriers with more than one waiting role exist once per chunk parity (..0/..1):
-// a parity wait only sees the current or the previous phase, so a waiter must
-// never fall two phases behind.  With one barrier per parity, the next completion
-// of each is causally behind the waiter's own progress.
 enum {
-    B_FULL0, B_FULL1, B_EMPTY0, B_EMPTY1, B_PREP0, B_PREP1, B_DFREE, B_IFULL, B_IEMPTY, B_SREADY0, B_SREADY1,
-    B_DSFULL, B_PREADY0, B_PREADY1, B_OFULL0, B_OFULL1, B_OEMPTY0, B_OEMPTY1, B_FINAL, NBAR
+    B_FULL0, B_FULL1, B_CDONE0, B_CDONE1, B_PREP0, B_PREP1, B_IFULL0, B_IFULL1, B_PREADY0, B_PREADY1, B_DSFULL,
+    B_SREADY, B_OEMPTY0, B_OEMPTY1, B_FINAL, NBAR
 };
 
 struct Small {
-    uint64_t bar[20];
+    uint64_t bar[16];
     float pw[C + 4];      // l^t, t = 0..C
     float geo[C + 4];     // sum_{t<n} l^t
-    float den[2][C];      // intra-chunk denominators (per chunk parity)
-    float cden[2][C];     // psi(q_i).[Z1;Z2] with the state entering the chunk
-    float s0f[2][D];      // S0 entering the chunk (float32)
-    float zf[2][F];       // [Z1; Z2] entering the chunk (float32)
-    float zsum[2][3 * D]; // per chunk: sum w v | sum w k | sum w k^2
-    float red[4][3 * D];  // per-warp partial column sums
+    float s0f[2][D];      // S0 entering the chunk (float32), per chunk parity
     uint32_t tmem_base;
     int abort_flag;
 };
 constexpr size_t SMEM_BYTES = OFF_SMALL + sizeof(Small) + 1024;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+static_assert(SimtSmem<64, 64>::bytes <= OFF_SMALL, "fallback path fits in the same allocation");
 
 // tensor-memory columns
-constexpr uint32_t T_A = 0, T_DS = 128, T_CARRY = 192, T_NUM = 320, T_COLS = 512;
+constexpr uint32_t T_A = 0, T_ACC = 256, T_DS = 384, T_DEN = 448, T_DZ = 480, T_DS0 = 496, T_COLS = 512;
 
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
 
@@ -92,11 +99,24 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *b) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t parity) {
+// may suspend the thread briefly while the phase is incomplete
+__device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// never blocks (the MMA issuer polls several barriers)
+__device__ __forceinline__ bool mbar_poll(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(su32(b)), "r"(parity)
@@ -109,22 +129,28 @@ struct Ctl {
     int *status;               // global: first failure code (nullable)
 };
 
-// Wait for the phase of parity `parity` to complete.  Bounded by WAIT_NS; on
-// expiry (or when another role already gave up) returns false.
-__device__ __noinline__ bool mbar_wait(uint64_t *b, uint32_t parity, const Ctl &ctl, int code) {
-    if (mbar_test(b, parity)) return true;
+__device__ __forceinline__ void give_up(const Ctl &ctl, int code) {
+    *ctl.abort_flag = 1;
+    if (ctl.status) atomicCAS(ctl.status, 0, code);
+}
+
+__device__ __noinline__ bool mbar_wait_slow(uint64_t *b, uint32_t parity, const Ctl &ctl, int code) {
     const unsigned long long t0 = gtimer();
     for (uint32_t it = 1;; ++it) {
-        if (mbar_test(b, parity)) return true;
-        if ((it & 255) == 0) {
+        if (mbar_try(b, parity)) return true;
+        if ((it & 63) == 0) {
             if (*ctl.abort_flag) return false;
             if (gtimer() - t0 > WAIT_NS) {
-                *ctl.abort_flag = 1;
-                if (ctl.status) atomicCAS(ctl.status, 0, code);
+                give_up(ctl, code);
                 return false;
             }
         }
     }
+}
+// Wait for the phase of parity `parity`; false if it timed out or another role gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, const Ctl &ctl, int code) {
+    if (mbar_try(b, parity)) return true;
+    return mbar_wait_slow(b, parity, ctl, code);
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -146,16 +172,25 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
 }
-// Instruction descriptor, kind::f16: bf16 x bf16 -> f32, dense.
+// Instruction descriptor, kind::f16: bf16 x bf16 -> f32, dense; a_mn/b_mn = operand is MN-major.
 __host__ __device__ constexpr uint32_t idesc(int M, int N, int a_mn, int b_mn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+// D (tmem) [+]= A (smem) B (smem)
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
         "l"(a), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+}
+// D (tmem) [+]= A (tmem, K-major) B (smem)
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a_tmem), "l"(b), "r"(id), "r"(acc)
         : "memory");
 }
 __device__ __forceinline__ void commit(uint64_t *bar) {
@@ -178,16 +213,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
-
-__device__ __forceinline__ void unpack8(const uint4 u, float *f) {
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
-        f[2 * i] = t.x;
-        f[2 * i + 1] = t.y;
-    }
+// One float32 column of this thread's TMEM lane.
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    return __uint_as_float(r);
 }
+// 16 consecutive 32-bit columns of this thread's TMEM lane (completion via tmem_wait_st).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&h);
@@ -195,8 +238,12 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 __device__ __forceinline__ uint4 pack8(const float *f) {
     return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
 }
+__device__ __forceinline__ __nv_bfloat162 as_b2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162 *>(&u); }
+__device__ __forceinline__ uint32_t as_u(__nv_bfloat162 h) { return *reinterpret_cast<uint32_t *>(&h); }
 // byte offset of 16-byte chunk `c` of row `r` in a [rows x 128 B] tile with the 128-byte swizzle
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+// byte offset of element k of row 0 in a one-row K-major tile (two 64-element atoms of 16 rows)
+__device__ __forceinline__ uint32_t row0(int k) { return (uint32_t)((k >> 6) * 2048 + (k & 63) * 2); }
 
 template <typename TO>
 __device__ __forceinline__ void store_row32(TO *dst, const float *v);
@@ -214,8 +261,8 @@ __device__ __forceinline__ void store_row32<float>(float *dst, const float *v) {
 }
 
 // ------------------------------------------------------------------ the kernel
-template <bool STATE_ONLY, typename TO>
-__global__ void __launch_bounds__(384, 1)
+template <bool SO, typename TO>   // SO: state only (no q, no output rows)
+__global__ void __launch_bounds__(512, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                       const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -226,19 +273,29 @@ __global__ void __launch_bounds__(384, 1)
     const int bh = blockIdx.x, seg = blockIdx.y;
     const int b = bh / p.H, h = bh - b * p.H;
     const float lam = p.lambda[(int64_t)b * p.lam_sb + h];
+
+    if (!(lam >= LMIN)) {  // small decay (or NaN): float32 CUDA-core chunk loop, whole CTA
+        simt_prefill_body<64, 64, __nv_bfloat16, TO>(p, reinterpret_cast<float *>(smem), bh, seg);
+        return;
+    }
+
     const int nchunks_total = (p.L + C - 1) / C;
     const int seg_chunks = p.seg_len / C;
     const int c_begin = seg * seg_chunks;
     const int c_end = min(c_begin + seg_chunks, nchunks_total);
     const int U = c_end - c_begin;
+    const int n_last = min(C, p.L - (c_end - 1) * C);
     Ctl ctl{&sm.abort_flag, p.status};
 
+    // ---- set-up: powers, barriers, constant one-row tiles, tensor memory
     if (threadIdx.x <= C) sm.pw[threadIdx.x] = (float)pow((double)lam, (double)threadIdx.x);
+    for (int i = threadIdx.x; i < 5 * ROW1 / 16; i += blockDim.x)  // zero ZT x2, W16 x2, ONES
+        reinterpret_cast<uint4 *>(smem + OFF_ZT)[i] = make_uint4(0u, 0u, 0u, 0u);
     if (threadIdx.x == 0) {
         for (int i = 0; i < NBAR; ++i) {
             uint32_t n = 1;
-            if (i == B_PREP0 || i == B_PREP1 || i == B_IEMPTY || i == B_SREADY0 || i == B_SREADY1 ||
-                i == B_PREADY0 || i == B_PREADY1 || i == B_OEMPTY0 || i == B_OEMPTY1)
+            if (i == B_PREP0 || i == B_PREP1 || i == B_PREADY0 || i == B_PREADY1 || i == B_SREADY ||
+                i == B_OEMPTY0 || i == B_OEMPTY1)
                 n = 128;
             mbar_init(&sm.bar[i], n);
         }
@@ -261,221 +318,246 @@ __global__ void __launch_bounds__(384, 1)
             if (j < C) g += sm.pw[j];
         }
     }
+    if (threadIdx.x < C) {  // w row for full chunks, and the ones row
+        const int j = threadIdx.x;
+        *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_W16 + row0(j)) = __float2bfloat16_rn(sm.pw[C - 1 - j]);
+        *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_ONES + row0(j)) = __float2bfloat16_rn(1.0f);
+    }
+    fence_proxy_async();
     __syncthreads();
     const uint32_t tmem = sm.tmem_base;
     uint64_t *bar = sm.bar;
 
     if (warp == 0) {
         // ============================== TMA producer
-        if (lane == 0 && U > 0) {
+        if (lane == 0) {
             int issued = 0;
             for (int u = 0; u < U; ++u) {
                 const int st = u & 1;
-                if (!mbar_wait(&bar[B_EMPTY0 + st], ((u >> 1) & 1) ^ 1, ctl, 1)) break;
+                if (!mbar_wait(&bar[B_CDONE0 + st], ((u >> 1) & 1) ^ 1, ctl, 1)) break;
                 const int t0 = (c_begin + u) * C;
                 uint8_t *base = smem + st * STAGE;
-                mbar_expect_tx(&bar[B_FULL0 + st], STATE_ONLY ? 2 * TILE : 3 * TILE);
-                if (!STATE_ONLY) tma_load(base, &tq, &bar[B_FULL0 + st], 0, t0, h, b);
+                mbar_expect_tx(&bar[B_FULL0 + st], SO ? 2 * TILE : 3 * TILE);
+                if (!SO) tma_load(base, &tq, &bar[B_FULL0 + st], 0, t0, h, b);
                 tma_load(base + TILE, &tk, &bar[B_FULL0 + st], 0, t0, h, b);
                 tma_load(base + 2 * TILE, &tv, &bar[B_FULL0 + st], 0, t0, h, b);
                 issued = u + 1;
             }
             // never leave with copies in flight: the last (up to) two stages must have landed
             for (int u = max(0, issued - 2); u < issued; ++u) {
-                const int st = u & 1;
                 const unsigned long long t0 = gtimer();
-                while (!mbar_test(&bar[B_FULL0 + st], (u >> 1) & 1) && gtimer() - t0 < WAIT_NS) {
+                while (!mbar_try(&bar[B_FULL0 + (u & 1)], (u >> 1) & 1) && gtimer() - t0 < WAIT_NS) {
                 }
             }
         }
     } else if (warp == 1) {
         // ============================== MMA issuer
-        if (lane == 0 && U > 0) {
-            constexpr uint32_t ID_A = idesc(128, 128, 0, 0);   // psi(Q) phi(K)^T: both K-major
-            constexpr uint32_t ID_DS = idesc(128, 64, 1, 1);   // phi(K)^T (w.V): both MN-major
-            constexpr uint32_t ID_C = idesc(128, 64, 0, 1);    // psi(Q) S / P V: A K-major, B MN-major
-            for (int u = 0; u < U; ++u) {
-                const int st = u & 1;
-                const uint32_t q_s = sb + st * STAGE, k_s = q_s + TILE, v_s = q_s + 2 * TILE;
-                const uint32_t ph = (u >> 1) & 1;  // phase parity of the per-parity barriers
-                if (!mbar_wait(&bar[B_PREP0 + st], ph, ctl, 2)) break;
-                if (!STATE_ONLY) {
-                    if (!mbar_wait(&bar[B_IEMPTY], (u & 1) ^ 1, ctl, 3)) break;
-                    tc_fence_after();
-                    // A = [Q | Q2] [K | K2]^T  (K-dim = features; 16 per instruction = 32 bytes)
+        if (lane == 0) {
+            constexpr uint32_t ID_A = idesc(128, 128, 0, 0);  // [Qg|Q2g][K|K2]^T
+            constexpr uint32_t ID_DS = idesc(128, 64, 1, 1);  // [K|K2]^T Vw
+            constexpr uint32_t ID_DZ = idesc(128, 16, 1, 0);  // [K|K2]^T w, [Vw|.]^T 1
+            constexpr uint32_t ID_C = idesc(128, 64, 0, 1);   // [Qg|Q2g][S1;S2], P' Vw
+            constexpr uint32_t ID_CZ = idesc(128, 16, 0, 0);  // [Qg|Q2g][Z1;Z2], P' w
+            int u1 = 0, u2 = 0, u4 = 0;
+            unsigned long long last = gtimer();
+            while (u2 < U || (!SO && u4 < U)) {
+                if (*ctl.abort_flag) break;
+                bool prog = false;
+                // ---- group 1: At = [Qg|Q2g][K|K2]^T into At[u1 & 1]
+                if (!SO && u1 < U) {
+                    const int bb = u1 & 1;
+                    if (mbar_poll(&bar[B_PREP0 + bb], (u1 >> 1) & 1) &&
+                        mbar_poll(&bar[B_CDONE0 + bb], ((u1 >> 1) & 1) ^ 1)) {
+                        tc_fence_after();
+                        const uint32_t q_s = sb + bb * STAGE, k_s = q_s + TILE;
+                        const uint32_t q2 = sb + OFF_DER + bb * 2 * TILE, k2 = q2 + TILE;
 #pragma unroll
-                    for (int s = 0; s < 8; ++s) {
-                        const uint32_t a = (s < 4 ? q_s : sb + OFF_Q2) + (s & 3) * 32;
-                        const uint32_t bb = (s < 4 ? k_s : sb + OFF_K2) + (s & 3) * 32;
-                        mma(tmem + T_A, sdesc(a, 16, 1024), sdesc(bb, 16, 1024), ID_A, s > 0);
-                    }
-                    commit(&bar[B_IFULL]);
-                }
-                if (!mbar_wait(&bar[B_SREADY0 + st], ph, ctl, 4)) break;
-                if (!STATE_ONLY && !mbar_wait(&bar[B_OEMPTY0 + st], ph ^ 1, ctl, 5)) break;
-                tc_fence_after();
-                // dS = [K | K2]^T (w.V): A MN-major (features contiguous), K and K2 tiles are the
-                // two 64-feature atoms (LBO = their distance); K-dim = tokens, 16 rows = 2048 B
-                {
-                    const uint32_t lbo = sb + OFF_K2 - k_s;
-#pragma unroll
-                    for (int s = 0; s < 8; ++s)
-                        mma(tmem + T_DS, sdesc(k_s + s * 2048, lbo, 1024), sdesc(sb + OFF_VW + s * 2048, 8192, 1024),
-                            ID_DS, s > 0);
-                }
-                commit(&bar[B_DSFULL]);
-                if (!STATE_ONLY) {
-                    // carry = [Q | Q2] [S1; S2] (state entering this chunk, bf16, [feature][value])
-                    const uint32_t sbuf = sb + OFF_SB + (u & 1) * TILE;
-                    const uint32_t tc_ = tmem + T_CARRY + st * 64;
-#pragma unroll
-                    for (int s = 0; s < 8; ++s) {
-                        const uint32_t a = (s < 4 ? q_s : sb + OFF_Q2) + (s & 3) * 32;
-                        mma(tc_, sdesc(a, 16, 1024), sdesc(sbuf + s * 2048, 8192, 1024), ID_C, s > 0);
+                        for (int s = 0; s < 8; ++s) {
+                            const uint32_t a = (s < 4 ? q_s : q2) + (s & 3) * 32;
+                            const uint32_t bv = (s < 4 ? k_s : k2) + (s & 3) * 32;
+                            mma_ss(tmem + T_A + bb * 128, sdesc(a, 16, 1024), sdesc(bv, 16, 1024), ID_A, s > 0);
+                        }
+                        commit(&bar[B_IFULL0 + bb]);
+                        ++u1;
+                        prog = true;
                     }
                 }
-                commit(&bar[B_DFREE]);
-                if (!STATE_ONLY) {
-                    if (!mbar_wait(&bar[B_PREADY0 + st], ph, ctl, 6)) break;
-                    tc_fence_after();
-                    // num = P V: P K-major in two 64-token atoms; V MN-major
-                    const uint32_t tn = tmem + T_NUM + st * 64;
+                // ---- group 2: state GEMMs of chunk u2 (+ carry GEMMs)
+                if (u2 < U && (SO || u2 < u1)) {
+                    const int bb = u2 & 1;
+                    if ((!SO || mbar_poll(&bar[B_PREP0 + bb], (u2 >> 1) & 1)) && mbar_poll(&bar[B_SREADY], u2 & 1) &&
+                        (SO || mbar_poll(&bar[B_OEMPTY0 + bb], ((u2 >> 1) & 1) ^ 1))) {
+                        tc_fence_after();
+                        const uint32_t q_s = sb + bb * STAGE, k_s = q_s + TILE, v_s = q_s + 2 * TILE;
+                        const uint32_t q2 = sb + OFF_DER + bb * 2 * TILE, k2 = q2 + TILE;
+                        const int n = (u2 == U - 1) ? n_last : C;
+                        const uint32_t w16 = sb + OFF_W16 + (n < C ? ROW1 : 0), ones = sb + OFF_ONES;
+                        const uint32_t lbo_k = k2 - k_s, lbo_v = k2 - v_s;
 #pragma unroll
-                    for (int s = 0; s < 8; ++s) {
-                        const uint32_t a = sb + OFF_P + (s >> 2) * TILE + (s & 3) * 32;
-                        mma(tn, sdesc(a, 16, 1024), sdesc(v_s + s * 2048, 8192, 1024), ID_C, s > 0);
+                        for (int s = 0; s < 8; ++s) {  // K-dim = tokens, 16 rows = 2048 B per step
+                            const uint32_t o = (s >> 2) * 2048 + (s & 3) * 32;
+                            mma_ss(tmem + T_DS, sdesc(k_s + s * 2048, lbo_k, 1024), sdesc(v_s + s * 2048, 8192, 1024),
+                                   ID_DS, s > 0);
+                            mma_ss(tmem + T_DZ, sdesc(k_s + s * 2048, lbo_k, 1024), sdesc(w16 + o, 16, 1024), ID_DZ,
+                                   s > 0);
+                            mma_ss(tmem + T_DS0, sdesc(v_s + s * 2048, lbo_v, 1024), sdesc(ones + o, 16, 1024), ID_DZ,
+                                   s > 0);
+                        }
+                        if (!SO) {
+                            const uint32_t sbuf = sb + OFF_SB + (u2 & 1) * TILE, zt = sb + OFF_ZT + (u2 & 1) * ROW1;
+#pragma unroll
+                            for (int s = 0; s < 8; ++s) {  // K-dim = features
+                                const uint32_t a = (s < 4 ? q_s : q2) + (s & 3) * 32;
+                                const uint32_t o = (s >> 2) * 2048 + (s & 3) * 32;
+                                mma_ss(tmem + T_ACC + bb * 64, sdesc(a, 16, 1024), sdesc(sbuf + s * 2048, 8192, 1024),
+                                       ID_C, s > 0);
+                                mma_ss(tmem + T_DEN + bb * 16, sdesc(a, 16, 1024), sdesc(zt + o, 16, 1024), ID_CZ,
+                                       s > 0);
+                            }
+                        }
+                        commit(&bar[B_DSFULL]);
+                        if (SO) commit(&bar[B_CDONE0 + bb]);
+                        ++u2;
+                        prog = true;
                     }
-                    commit(&bar[B_OFULL0 + st]);
                 }
-                commit(&bar[B_EMPTY0 + st]);
+                // ---- group 4: ACC += P' Vw, DEN += P' w  (P' from tensor memory)
+                if (!SO && u4 < u2) {
+                    const int bb = u4 & 1;
+                    if (mbar_poll(&bar[B_PREADY0 + bb], (u4 >> 1) & 1)) {
+                        tc_fence_after();
+                        const uint32_t v_s = sb + bb * STAGE + 2 * TILE;
+                        const int n = (u4 == U - 1) ? n_last : C;
+                        const uint32_t w16 = sb + OFF_W16 + (n < C ? ROW1 : 0);
+#pragma unroll
+                        for (int s = 0; s < 8; ++s) {  // K-dim = tokens; P' packs 2 per column
+                            const uint32_t pa = tmem + T_A + bb * 128 + s * 8;
+                            mma_ts(tmem + T_ACC + bb * 64, pa, sdesc(v_s + s * 2048, 8192, 1024), ID_C, 1);
+                            mma_ts(tmem + T_DEN + bb * 16, pa, sdesc(w16 + (s >> 2) * 2048 + (s & 3) * 32, 16, 1024),
+                                   ID_CZ, 1);
+                        }
+                        commit(&bar[B_CDONE0 + bb]);
+                        ++u4;
+                        prog = true;
+                    }
+                }
+                if (prog) {
+                    last = gtimer();
+                } else {
+                    if (gtimer() - last > WAIT_NS) {
+                        give_up(ctl, 2);
+                        break;
+                    }
+                    __nanosleep(32);
+                }
             }
             // every GEMM issued must be complete before tensor memory is released
             commit(&bar[B_FINAL]);
             const unsigned long long t0 = gtimer();
-            while (!mbar_test(&bar[B_FINAL], 0) && gtimer() - t0 < WAIT_NS) {
+            while (!mbar_try(&bar[B_FINAL], 0) && gtimer() - t0 < WAIT_NS) {
             }
         }
     } else if (warp >= 4 && warp < 8) {
-        // ============================== prep + decay-mask epilogue
-        const int tid = threadIdx.x - 128, wq = warp - 4;
-        const int cc = tid & 7, rb = tid >> 3;   // prep: 16-byte column chunk, block of 8 rows
-        const int i = wq * 32 + lane;            // epilogue: token row (TMEM lane)
+        // ============================== prep: Qg (in place), Q2g, K^2 (new tiles), Vw (in place)
+        const int tid = threadIdx.x - 128;
+        const int cc = tid & 7, rb = tid >> 3;  // one 16-byte column chunk of 8 rows
+        __nv_bfloat162 gq[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) gq[t] = __float2bfloat162_rn(sm.pw[rb * 8 + t + 1]);
+        const __nv_bfloat162 half2 = __float2bfloat162_rn(0.5f);
         for (int u = 0; u < U; ++u) {
             const int st = u & 1;
-            const int t0 = (c_begin + u) * C;
-            const int n = min(C, p.L - t0);
-            uint8_t *q_s = smem + st * STAGE, *k_s = q_s + TILE, *v_s = q_s + 2 * TILE;
+            const int n = (u == U - 1) ? n_last : C;
             if (!mbar_wait(&bar[B_FULL0 + st], (u >> 1) & 1, ctl, 7)) break;
-            if (!mbar_wait(&bar[B_DFREE], (u & 1) ^ 1, ctl, 8)) break;
-            // ---- prep: 8 rows x one 16-byte chunk per tile
-            float zv[8], zk[8], zk2[8];
+            if (!mbar_wait(&bar[B_CDONE0 + st], ((u >> 1) & 1) ^ 1, ctl, 8)) break;
+            uint8_t *q_s = smem + st * STAGE, *k_s = q_s + TILE, *v_s = q_s + 2 * TILE;
+            uint8_t *q2 = smem + OFF_DER + st * 2 * TILE, *k2 = q2 + TILE;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) zv[c] = zk[c] = zk2[c] = 0.f;
-#pragma unroll 2
             for (int t = 0; t < 8; ++t) {
                 const int r = rb * 8 + t;
                 const uint32_t off = swz(r, cc);
-                const float w = r < n ? sm.pw[n - 1 - r] : 0.f;
-                float x[8], o[8];
-                if (!STATE_ONLY) {
-                    unpack8(*reinterpret_cast<const uint4 *>(q_s + off), x);
+                const __nv_bfloat162 ww = __float2bfloat162_rn(r < n ? sm.pw[n - 1 - r] : 0.f);
+                if (!SO) {
+                    const uint4 x = *reinterpret_cast<const uint4 *>(q_s + off);
+                    uint32_t xq[4] = {x.x, x.y, x.z, x.w}, yq[4];
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) o[c] = 0.5f * x[c] * x[c];
-                    *reinterpret_cast<uint4 *>(smem + OFF_Q2 + off) = pack8(o);
+                    for (int c = 0; c < 4; ++c) {
+                        const __nv_bfloat162 qv = as_b2(xq[c]);
+                        const __nv_bfloat162 qg = __hmul2(qv, gq[t]);
+                        yq[c] = as_u(__hmul2(qg, __hmul2(qv, half2)));
+                        xq[c] = as_u(qg);
+                    }
+                    *reinterpret_cast<uint4 *>(q_s + off) = make_uint4(xq[0], xq[1], xq[2], xq[3]);
+                    *reinterpret_cast<uint4 *>(q2 + off) = make_uint4(yq[0], yq[1], yq[2], yq[3]);
                 }
-                unpack8(*reinterpret_cast<const uint4 *>(k_s + off), x);
+                {
+                    const uint4 x = *reinterpret_cast<const uint4 *>(k_s + off);
+                    const uint32_t xk[4] = {x.x, x.y, x.z, x.w};
+                    uint32_t yk[4];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    o[c] = x[c] * x[c];
-                    zk[c] = fmaf(w, x[c], zk[c]);
-                    zk2[c] = fmaf(w, o[c], zk2[c]);
+                    for (int c = 0; c < 4; ++c) yk[c] = as_u(__hmul2(as_b2(xk[c]), as_b2(xk[c])));
+                    *reinterpret_cast<uint4 *>(k2 + off) = make_uint4(yk[0], yk[1], yk[2], yk[3]);
                 }
-                *reinterpret_cast<uint4 *>(smem + OFF_K2 + off) = pack8(o);
-                unpack8(*reinterpret_cast<const uint4 *>(v_s + off), x);
+                {
+                    const uint4 x = *reinterpret_cast<const uint4 *>(v_s + off);
+                    const uint32_t xv[4] = {x.x, x.y, x.z, x.w};
+                    uint32_t yv[4];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    o[c] = w * x[c];
-                    zv[c] += o[c];
-                }
-                *reinterpret_cast<uint4 *>(smem + OFF_VW + off) = pack8(o);
-            }
-            // column sums: lanes sharing a chunk are lane ^ 8, lane ^ 16
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-#pragma unroll
-                for (int o = 8; o <= 16; o <<= 1) {
-                    zv[c] += __shfl_xor_sync(0xffffffffu, zv[c], o);
-                    zk[c] += __shfl_xor_sync(0xffffffffu, zk[c], o);
-                    zk2[c] += __shfl_xor_sync(0xffffffffu, zk2[c], o);
+                    for (int c = 0; c < 4; ++c) yv[c] = as_u(__hmul2(as_b2(xv[c]), ww));
+                    *reinterpret_cast<uint4 *>(v_s + off) = make_uint4(yv[0], yv[1], yv[2], yv[3]);
                 }
             }
-            named_bar(1, 128);  // the previous chunk's readers of red[] are done
-            if (lane < 8) {
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    sm.red[wq][cc * 8 + c] = zv[c];
-                    sm.red[wq][D + cc * 8 + c] = zk[c];
-                    sm.red[wq][2 * D + cc * 8 + c] = zk2[c];
-                }
-            }
-            named_bar(1, 128);
-            for (int idx = tid; idx < 3 * D; idx += 128)
-                sm.zsum[st][idx] = sm.red[0][idx] + sm.red[1][idx] + sm.red[2][idx] + sm.red[3][idx];
+            if (u == U - 1 && n < C)  // w row of the partial last chunk
+                *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_W16 + ROW1 + row0(tid)) =
+                    __float2bfloat16_rn(tid < n ? sm.pw[n - 1 - tid] : 0.f);
             fence_proxy_async();
             mbar_arrive(&bar[B_PREP0 + st]);
-            if (STATE_ONLY) continue;
-
-            // ---- decay mask: P[i][j] = l^(i-j) (1 + A[i][j]) for j <= i
-            if (!mbar_wait(&bar[B_IFULL], u & 1, ctl, 9)) break;
-            tc_fence_after();
-            float den = 0.f;
-#pragma unroll 1
-            for (int g = 0; g < 4; ++g) {
-                uint8_t *prow = smem + OFF_P + (g >> 1) * TILE;
-                if (g > wq) {  // whole 32-column group above the diagonal for this warp
-                    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) *reinterpret_cast<uint4 *>(prow + swz(i, 4 * (g & 1) + c4)) = z;
-                    continue;
-                }
-                float a[32];
-                tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + T_A + 32 * g, a);
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) {
-                    const int j = 32 * g + jj;
-                    float pv = 0.f;
-                    if (j <= i) pv = sm.pw[i - j] * (1.0f + a[jj]);
-                    a[jj] = pv;
-                    den += pv;
-                }
-#pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4)
-                    *reinterpret_cast<uint4 *>(prow + swz(i, 4 * (g & 1) + c4)) = pack8(a + 8 * c4);
-            }
-            fence_proxy_async();
-            tc_fence_before();
-            mbar_arrive(&bar[B_IEMPTY]);
-            // carried denominator needs the state entering this chunk
-            if (!mbar_wait(&bar[B_SREADY0 + st], (u >> 1) & 1, ctl, 10)) break;
-            float cd = 0.f;
-            {
-                const float *z1 = sm.zf[st], *z2 = sm.zf[st] + D;
-#pragma unroll 2
-                for (int c = 0; c < 8; ++c) {
-                    float x[8];
-                    unpack8(*reinterpret_cast<const uint4 *>(q_s + swz(i, c)), x);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) cd = fmaf(x[e], z1[8 * c + e], fmaf(0.5f * x[e] * x[e], z2[8 * c + e], cd));
-                }
-            }
-            if (!mbar_wait(&bar[B_OEMPTY0 + st], ((u >> 1) & 1) ^ 1, ctl, 11)) break;
-            sm.den[st][i] = den;
-            sm.cden[st][i] = cd;
-            mbar_arrive(&bar[B_PREADY0 + st]);
         }
-    } else if (warp >= 8) {
-        // ============================== state update + output epilogue
-        const int wq = warp - 8;
+    } else if (warp >= 8 && warp < 12) {
+        // ============================== mask: At -> P' = l^(i-n+1) + l^-n At (j <= i), in tensor memory
+        if (!SO) {
+            const int wq = warp - 8;
+            const int i = wq * 32 + lane;
+            const uint32_t lane_base = tmem + ((uint32_t)(wq * 32) << 16);
+            for (int u = 0; u < U; ++u) {
+                const int bb = u & 1;
+                const int n = (u == U - 1) ? n_last : C;
+                const float cn = 1.0f / sm.pw[n];        // l^-n
+                const float ri = sm.pw[i + 1] * cn;      // l^(i+1-n)
+                if (!mbar_wait(&bar[B_IFULL0 + bb], (u >> 1) & 1, ctl, 9)) break;
+                tc_fence_after();
+                const uint32_t abase = lane_base + T_A + bb * 128;
+#pragma unroll 1
+                for (int g = 0; g < 4; ++g) {
+                    uint32_t pk[16];
+                    if (g > wq) {  // columns above the diagonal for every row of this warp
+#pragma unroll
+                        for (int c = 0; c < 16; ++c) pk[c] = 0u;
+                    } else {
+                        float a[32];
+                        tmem_ld32(abase + 32 * g, a);
+                        if (g < wq) {
+#pragma unroll
+                            for (int c = 0; c < 16; ++c)
+                                pk[c] = pack2(fmaf(cn, a[2 * c], ri), fmaf(cn, a[2 * c + 1], ri));
+                        } else {
+#pragma unroll
+                            for (int c = 0; c < 16; ++c)
+                                pk[c] = pack2(2 * c <= lane ? fmaf(cn, a[2 * c], ri) : 0.f,
+                                              2 * c + 1 <= lane ? fmaf(cn, a[2 * c + 1], ri) : 0.f);
+                        }
+                    }
+                    // P' of columns 32g..32g+31 -> columns 16g..16g+15, whose At values were already read
+                    tmem_st16(abase + 16 * g, pk);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&bar[B_PREADY0 + bb]);
+            }
+        }
+    } else if (warp >= 12) {
+        // ============================== state update + output rows
+        const int wq = warp - 12;
         const int f = wq * 32 + lane;  // feature row for the state, token row for the output
         const uint32_t lane_base = tmem + ((uint32_t)(wq * 32) << 16);
         float S[D];
@@ -503,29 +585,29 @@ __global__ void __launch_bounds__(384, 1)
             Z = 0.f;
             Z0 = 0.f;
         }
-        auto publish = [&](int buf) {  // bf16 state tile + float32 vectors for the next chunk
+        auto publish = [&](int buf) {  // bf16 [S1;S2] row f, [Z1;Z2] element f, S0 for the next chunk
             uint8_t *srow = smem + OFF_SB + buf * TILE;
 #pragma unroll
             for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4 *>(srow + swz(f, c)) = pack8(S + 8 * c);
-            sm.zf[buf][f] = Z;
+            *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_ZT + buf * ROW1 + row0(f)) = __float2bfloat16_rn(Z);
             if (f < D) sm.s0f[buf][f] = s0;
         };
-        if (!STATE_ONLY) publish(0);
+        if (!SO) publish(0);
         fence_proxy_async();
         tc_fence_before();
-        mbar_arrive(&bar[B_SREADY0]);
+        mbar_arrive(&bar[B_SREADY]);
         bool ok = true;
         for (int u = 0; u < U && ok; ++u) {
-            const int st = u & 1;
+            const int bb = u & 1;
             const int t0 = (c_begin + u) * C;
-            const int n = min(C, p.L - t0);
+            const int n = (u == U - 1) ? n_last : C;
             // ---- state update
-            if (!mbar_wait(&bar[B_DSFULL], u & 1, ctl, 12) || !mbar_wait(&bar[B_PREP0 + st], (u >> 1) & 1, ctl, 13)) {
+            if (!mbar_wait(&bar[B_DSFULL], u & 1, ctl, 12)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            named_bar(2, 128);  // every thread finished reading the buffers about to be rewritten
+            named_bar(2, 128);  // all rows of the previous chunk's output read s0f[bb ^ 1]
             const float decay = sm.pw[n];
 #pragma unroll
             for (int hcol = 0; hcol < 2; ++hcol) {
@@ -534,39 +616,37 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                 for (int e = 0; e < 32; ++e) S[32 * hcol + e] = fmaf(decay, S[32 * hcol + e], d[e]);
             }
-            Z = fmaf(decay, Z, sm.zsum[st][D + f]);
-            if (f < D) s0 = fmaf(decay, s0, sm.zsum[st][f]);
+            Z = fmaf(decay, Z, tmem_ld1(lane_base + T_DZ));
+            const float ds0 = tmem_ld1(lane_base + T_DS0);
+            if (f < D) s0 = fmaf(decay, s0, ds0);
             const float Z0_in = Z0;
             Z0 = fmaf(decay, Z0, sm.geo[n]);
-            if (!STATE_ONLY) publish(st ^ 1);
+            if (!SO) publish(bb ^ 1);
             fence_proxy_async();
             tc_fence_before();
-            mbar_arrive(&bar[B_SREADY0 + (st ^ 1)]);
-            if (STATE_ONLY) continue;
+            mbar_arrive(&bar[B_SREADY]);
+            if (SO) continue;
             // ---- output rows
-            if (!mbar_wait(&bar[B_OFULL0 + st], (u >> 1) & 1, ctl, 14) ||
-                !mbar_wait(&bar[B_PREADY0 + st], (u >> 1) & 1, ctl, 15)) {
+            if (!mbar_wait(&bar[B_CDONE0 + bb], (u >> 1) & 1, ctl, 14)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const int i = f;
             const float g = sm.pw[i + 1];
-            const float dd = fmaxf(sm.den[st][i] + g * (Z0_in + sm.cden[st][i]), p.eps);
-            const float inv = 1.0f / dd;
+            const float inv = 1.0f / fmaxf(tmem_ld1(lane_base + T_DEN + bb * 16) + g * Z0_in, p.eps);
             TO *yrow = reinterpret_cast<TO *>(p.y.p) + b * p.y.sb + h * p.y.sh + (int64_t)(t0 + i) * p.y.sl;
-            const float *s0in = sm.s0f[st];
+            const float *s0in = sm.s0f[bb];
 #pragma unroll
             for (int hcol = 0; hcol < 2; ++hcol) {
-                float cr[32], nm[32];
-                tmem_ld32(lane_base + T_CARRY + st * 64 + 32 * hcol, cr);
-                tmem_ld32(lane_base + T_NUM + st * 64 + 32 * hcol, nm);
+                float acc[32];
+                tmem_ld32(lane_base + T_ACC + bb * 64 + 32 * hcol, acc);
 #pragma unroll
-                for (int e = 0; e < 32; ++e) nm[e] = (nm[e] + g * (s0in[32 * hcol + e] + cr[e])) * inv;
-                if (i < n) store_row32<TO>(yrow + 32 * hcol, nm);
+                for (int e = 0; e < 32; ++e) acc[e] = fmaf(g, s0in[32 * hcol + e], acc[e]) * inv;
+                if (i < n) store_row32<TO>(yrow + 32 * hcol, acc);
             }
             tc_fence_before();
-            mbar_arrive(&bar[B_OEMPTY0 + st]);
+            mbar_arrive(&bar[B_OEMPTY0 + bb]);
         }
         // ---- final state
         const bool write_out = ok && !*ctl.abort_flag && p.out.present() &&
@@ -640,7 +720,7 @@ static cudaError_t launch_t(const CUtensorMap &mq, const CUtensorMap &mk, const 
     auto kern = prefill_tc_kernel<SO, TO>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    kern<<<grid, 384, SMEM_BYTES, st>>>(mq, mk, mv, p);
+    kern<<<grid, 512, SMEM_BYTES, st>>>(mq, mk, mv, p);
     return cudaGetLastError();
 }
 
