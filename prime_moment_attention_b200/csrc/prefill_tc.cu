@@ -23,15 +23,20 @@
 // Data: q/k/v chunk tiles arrive by TMA (4-D tensor maps over the strided
 // tensors, 128-byte swizzle) into two stages; prep overwrites q by Qg and v by
 // Vw in place and writes Q2g and K^2 to double-buffered tiles.  Accumulators
-// live in tensor memory (512 columns): At x2 (P' is written back over the
-// consumed At columns and read by the P'-GEMMs from TMEM), ACC x2, dS, DEN x2,
-// dZ, dS0.  The bf16 state copy [S1; S2] and the one-row [Z1; Z2] tile that feed
-// the carry GEMMs are double-buffered.
+// live in tensor memory: At x2 (P' is written back over the consumed At columns
+// and read by the P'-GEMMs from TMEM), ACC x2, dS, DEN x2, and [dZ | dS0] in one
+// 16-column region.  The producer also prefetches the tiles of later chunks
+// into L2, so each stage load finds its data there.  The bf16 state copy
+// [S1; S2] and the one-row [Z1; Z2] tile that feed the carry GEMMs are
+// double-buffered.
 //
 // Warp roles (512 threads, one CTA per SM):
 //   warp 0        TMA producer
 //   warp 1        MMA issuer (one thread, event driven: issues each chunk's GEMM
-//                 groups as soon as their inputs are ready) and TMEM owner
+//                 groups as soon as their inputs are ready) and TMEM owner.  The
+//                 state GEMMs of chunk u+1 start as soon as the state warpgroup
+//                 has read dS of chunk u, so the recurrence's critical path is
+//                 one tensor-memory read, the dS GEMMs and one barrier hop.
 //   warps 4-7     prep: Qg, Q2g, K^2, Vw for each chunk
 //   warps 8-11    mask: At -> P' in tensor memory
 //   warps 12-15   state and output: S += dS (thread f owns feature row f), bf16
@@ -56,20 +61,21 @@ constexpr int OFF_SB = OFF_DER + 4 * TILE;    // bf16 [S1; S2], [128 features][6
 constexpr int ROW1 = 4096;                // one-row K-major tile: 2 atoms x 16 rows x 128 B
 constexpr int OFF_ZT = OFF_SB + 2 * TILE;     // [Z1; Z2] row, x2
 constexpr int OFF_W16 = OFF_ZT + 2 * ROW1;    // w row: full chunks, last partial chunk
-constexpr int OFF_ONES = OFF_W16 + 2 * ROW1;  // ones row
+constexpr int OFF_ONES = OFF_W16 + 2 * ROW1;  // ones in row 1 (dS0 lands in column 1 of [dZ | dS0])
+constexpr int PREFETCH = 3;               // chunks of L2 prefetch ahead of the stage loads
 constexpr int OFF_SMALL = OFF_ONES + ROW1;
 constexpr float LMIN = 0.55f;             // smallest decay the rescaled operands serve
 
 enum {
     B_FULL0, B_FULL1, B_CDONE0, B_CDONE1, B_PREP0, B_PREP1, B_IFULL0, B_IFULL1, B_PREADY0, B_PREADY1, B_DSFULL,
-    B_SREADY, B_OEMPTY0, B_OEMPTY1, B_FINAL, NBAR
+    B_DSFREE, B_SREADY0, B_SREADY1, B_OEMPTY0, B_OEMPTY1, B_FINAL, NBAR
 };
 
 struct Small {
-    uint64_t bar[16];
+    uint64_t bar[18];
     float pw[C + 4];      // l^t, t = 0..C
     float geo[C + 4];     // sum_{t<n} l^t
-    float s0f[2][D];      // S0 entering the chunk (float32), per chunk parity
+    alignas(16) float s0f[2][D];  // S0 entering the chunk (float32), per chunk parity
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -78,7 +84,7 @@ static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 static_assert(SimtSmem<64, 64>::bytes <= OFF_SMALL, "fallback path fits in the same allocation");
 
 // tensor-memory columns
-constexpr uint32_t T_A = 0, T_ACC = 256, T_DS = 384, T_DEN = 448, T_DZ = 480, T_DS0 = 496, T_COLS = 512;
+constexpr uint32_t T_A = 0, T_ACC = 256, T_DS = 384, T_DEN = 448, T_DZS = 480, T_COLS = 512;
 
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
 
@@ -167,6 +173,12 @@ __device__ __forceinline__ void tma_load(void *dst, const CUtensorMap *map, uint
         : "memory");
 }
 
+__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap *map, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(map), "r"(c0),
+                 "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+
 // Shared-memory matrix descriptor: 128-byte swizzle, sm_100 version field.
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
@@ -219,6 +231,13 @@ __device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
     return __uint_as_float(r);
+}
+// Two float32 columns of this thread's TMEM lane.
+__device__ __forceinline__ float2 tmem_ld2(uint32_t taddr) {
+    uint32_t r0, r1;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    return make_float2(__uint_as_float(r0), __uint_as_float(r1));
 }
 // 16 consecutive 32-bit columns of this thread's TMEM lane (completion via tmem_wait_st).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
@@ -294,8 +313,8 @@ __global__ void __launch_bounds__(512, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < NBAR; ++i) {
             uint32_t n = 1;
-            if (i == B_PREP0 || i == B_PREP1 || i == B_PREADY0 || i == B_PREADY1 || i == B_SREADY ||
-                i == B_OEMPTY0 || i == B_OEMPTY1)
+            if (i == B_PREP0 || i == B_PREP1 || i == B_PREADY0 || i == B_PREADY1 || i == B_SREADY0 ||
+                i == B_SREADY1 || i == B_DSFREE || i == B_OEMPTY0 || i == B_OEMPTY1)
                 n = 128;
             mbar_init(&sm.bar[i], n);
         }
@@ -321,7 +340,7 @@ __global__ void __launch_bounds__(512, 1)
     if (threadIdx.x < C) {  // w row for full chunks, and the ones row
         const int j = threadIdx.x;
         *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_W16 + row0(j)) = __float2bfloat16_rn(sm.pw[C - 1 - j]);
-        *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_ONES + row0(j)) = __float2bfloat16_rn(1.0f);
+        *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_ONES + 128 + row0(j)) = __float2bfloat16_rn(1.0f);
     }
     fence_proxy_async();
     __syncthreads();
@@ -331,8 +350,14 @@ __global__ void __launch_bounds__(512, 1)
     if (warp == 0) {
         // ============================== TMA producer
         if (lane == 0) {
-            int issued = 0;
+            int issued = 0, fetched = 0;
             for (int u = 0; u < U; ++u) {
+                for (; fetched < U && fetched <= u + PREFETCH; ++fetched) {
+                    const int tf = (c_begin + fetched) * C;
+                    if (!SO) tma_prefetch_l2(&tq, 0, tf, h, b);
+                    tma_prefetch_l2(&tk, 0, tf, h, b);
+                    tma_prefetch_l2(&tv, 0, tf, h, b);
+                }
                 const int st = u & 1;
                 if (!mbar_wait(&bar[B_CDONE0 + st], ((u >> 1) & 1) ^ 1, ctl, 1)) break;
                 const int t0 = (c_begin + u) * C;
@@ -358,9 +383,39 @@ __global__ void __launch_bounds__(512, 1)
             constexpr uint32_t ID_DZ = idesc(128, 16, 1, 0);  // [K|K2]^T w, [Vw|.]^T 1
             constexpr uint32_t ID_C = idesc(128, 64, 0, 1);   // [Qg|Q2g][S1;S2], P' Vw
             constexpr uint32_t ID_CZ = idesc(128, 16, 0, 0);  // [Qg|Q2g][Z1;Z2], P' w
-            int u1 = 0, u2 = 0, u4 = 0;
+            // Every operand descriptor is built once; a k-step only adds a constant to its start
+            // address field (the issue loop is what bounds a single-thread MMA issuer).
+            // (pairs per buffer; a ternary select keeps them in registers)
+            struct D2 {
+                uint64_t v0, v1;
+                __device__ __forceinline__ uint64_t operator[](int b) const { return b ? v1 : v0; }
+            };
+            auto mk = [&](auto f) { return D2{f(0), f(1)}; };
+            const uint32_t st1 = STAGE, der1 = 2 * TILE;
+            const D2 dQ = mk([&](int b) { return sdesc(sb + b * st1, 16, 1024); });
+            const D2 dQ2 = mk([&](int b) { return sdesc(sb + OFF_DER + b * der1, 16, 1024); });
+            const D2 dK = mk([&](int b) { return sdesc(sb + b * st1 + TILE, 16, 1024); });
+            const D2 dK2 = mk([&](int b) { return sdesc(sb + OFF_DER + b * der1 + TILE, 16, 1024); });
+            // [K | K2] and [Vw | K2] as MN-major A operands: two 64-row atoms, LBO = distance to K2
+            const D2 dKmn = mk([&](int b) {
+                return sdesc(sb + b * st1 + TILE, (OFF_DER + b * der1 + TILE) - (b * st1 + TILE), 1024);
+            });
+            const D2 dVmn = mk([&](int b) {
+                return sdesc(sb + b * st1 + 2 * TILE, (OFF_DER + b * der1 + TILE) - (b * st1 + 2 * TILE), 1024);
+            });
+            const D2 dV = mk([&](int b) { return sdesc(sb + b * st1 + 2 * TILE, 8192, 1024); });
+            const D2 dSB = mk([&](int b) { return sdesc(sb + OFF_SB + b * TILE, 8192, 1024); });
+            const D2 dZT = mk([&](int b) { return sdesc(sb + OFF_ZT + b * ROW1, 16, 1024); });
+            const D2 dW = mk([&](int b) { return sdesc(sb + OFF_W16 + b * ROW1, 16, 1024); });
+            const uint64_t dONES = sdesc(sb + OFF_ONES, 16, 1024);
+            // descriptor start-address steps (16-byte units) of k-step s
+            auto kmaj = [](int s) { return (uint64_t)((s & 3) * 2); };                  // +32 B in a 128 B row
+            auto mnmaj = [](int s) { return (uint64_t)(s * 128); };                     // +16 rows of 128 B
+            auto row1 = [](int s) { return (uint64_t)((s >> 2) * 128 + (s & 3) * 2); };  // one-row K-major tile
+            int u1 = 0, u2a = 0, u2b = 0, u4 = 0;
+            const int U2b = SO ? 0 : U;
             unsigned long long last = gtimer();
-            while (u2 < U || (!SO && u4 < U)) {
+            while (u2a < U || u2b < U2b || (!SO && u4 < U)) {
                 if (*ctl.abort_flag) break;
                 bool prog = false;
                 // ---- group 1: At = [Qg|Q2g][K|K2]^T into At[u1 & 1]
@@ -369,72 +424,66 @@ __global__ void __launch_bounds__(512, 1)
                     if (mbar_poll(&bar[B_PREP0 + bb], (u1 >> 1) & 1) &&
                         mbar_poll(&bar[B_CDONE0 + bb], ((u1 >> 1) & 1) ^ 1)) {
                         tc_fence_after();
-                        const uint32_t q_s = sb + bb * STAGE, k_s = q_s + TILE;
-                        const uint32_t q2 = sb + OFF_DER + bb * 2 * TILE, k2 = q2 + TILE;
 #pragma unroll
-                        for (int s = 0; s < 8; ++s) {
-                            const uint32_t a = (s < 4 ? q_s : q2) + (s & 3) * 32;
-                            const uint32_t bv = (s < 4 ? k_s : k2) + (s & 3) * 32;
-                            mma_ss(tmem + T_A + bb * 128, sdesc(a, 16, 1024), sdesc(bv, 16, 1024), ID_A, s > 0);
-                        }
+                        for (int s = 0; s < 8; ++s)
+                            mma_ss(tmem + T_A + bb * 128, (s < 4 ? dQ[bb] : dQ2[bb]) + kmaj(s),
+                                   (s < 4 ? dK[bb] : dK2[bb]) + kmaj(s), ID_A, s > 0);
                         commit(&bar[B_IFULL0 + bb]);
                         ++u1;
                         prog = true;
                     }
                 }
-                // ---- group 2: state GEMMs of chunk u2 (+ carry GEMMs)
-                if (u2 < U && (SO || u2 < u1)) {
-                    const int bb = u2 & 1;
-                    if ((!SO || mbar_poll(&bar[B_PREP0 + bb], (u2 >> 1) & 1)) && mbar_poll(&bar[B_SREADY], u2 & 1) &&
-                        (SO || mbar_poll(&bar[B_OEMPTY0 + bb], ((u2 >> 1) & 1) ^ 1))) {
+                // ---- group 2a: dS = [K|K2]^T Vw, [dZ | dS0] of chunk u2a.  Needs the state warpgroup
+                // to have read dS of the previous chunk, and (for the bf16 state buffers' reuse)
+                // the previous chunk's carry GEMMs issued before it.
+                if (u2a < U && (SO || u2a <= u2b)) {
+                    const int bb = u2a & 1;
+                    if (mbar_poll(&bar[B_PREP0 + bb], (u2a >> 1) & 1) && mbar_poll(&bar[B_DSFREE], u2a & 1)) {
                         tc_fence_after();
-                        const uint32_t q_s = sb + bb * STAGE, k_s = q_s + TILE, v_s = q_s + 2 * TILE;
-                        const uint32_t q2 = sb + OFF_DER + bb * 2 * TILE, k2 = q2 + TILE;
-                        const int n = (u2 == U - 1) ? n_last : C;
-                        const uint32_t w16 = sb + OFF_W16 + (n < C ? ROW1 : 0), ones = sb + OFF_ONES;
-                        const uint32_t lbo_k = k2 - k_s, lbo_v = k2 - v_s;
+                        const int n = (u2a == U - 1) ? n_last : C;
+                        const uint64_t dw = dW[n < C ? 1 : 0];
 #pragma unroll
                         for (int s = 0; s < 8; ++s) {  // K-dim = tokens, 16 rows = 2048 B per step
-                            const uint32_t o = (s >> 2) * 2048 + (s & 3) * 32;
-                            mma_ss(tmem + T_DS, sdesc(k_s + s * 2048, lbo_k, 1024), sdesc(v_s + s * 2048, 8192, 1024),
-                                   ID_DS, s > 0);
-                            mma_ss(tmem + T_DZ, sdesc(k_s + s * 2048, lbo_k, 1024), sdesc(w16 + o, 16, 1024), ID_DZ,
-                                   s > 0);
-                            mma_ss(tmem + T_DS0, sdesc(v_s + s * 2048, lbo_v, 1024), sdesc(ones + o, 16, 1024), ID_DZ,
-                                   s > 0);
+                            mma_ss(tmem + T_DS, dKmn[bb] + mnmaj(s), dV[bb] + mnmaj(s), ID_DS, s > 0);
+                            mma_ss(tmem + T_DZS, dKmn[bb] + mnmaj(s), dw + row1(s), ID_DZ, s > 0);
                         }
-                        if (!SO) {
-                            const uint32_t sbuf = sb + OFF_SB + (u2 & 1) * TILE, zt = sb + OFF_ZT + (u2 & 1) * ROW1;
 #pragma unroll
-                            for (int s = 0; s < 8; ++s) {  // K-dim = features
-                                const uint32_t a = (s < 4 ? q_s : q2) + (s & 3) * 32;
-                                const uint32_t o = (s >> 2) * 2048 + (s & 3) * 32;
-                                mma_ss(tmem + T_ACC + bb * 64, sdesc(a, 16, 1024), sdesc(sbuf + s * 2048, 8192, 1024),
-                                       ID_C, s > 0);
-                                mma_ss(tmem + T_DEN + bb * 16, sdesc(a, 16, 1024), sdesc(zt + o, 16, 1024), ID_CZ,
-                                       s > 0);
-                            }
-                        }
+                        for (int s = 0; s < 8; ++s)  // column 1 of [dZ | dS0]: ones sit in row 1 of their tile
+                            mma_ss(tmem + T_DZS, dVmn[bb] + mnmaj(s), dONES + row1(s), ID_DZ, 1);
                         commit(&bar[B_DSFULL]);
                         if (SO) commit(&bar[B_CDONE0 + bb]);
-                        ++u2;
+                        ++u2a;
+                        prog = true;
+                    }
+                }
+                // ---- group 2b: carry GEMMs of chunk u2b with the state entering it
+                if (!SO && u2b < u2a && u2b < u1) {
+                    const int bb = u2b & 1;
+                    if (mbar_poll(&bar[B_SREADY0 + bb], (u2b >> 1) & 1) &&
+                        mbar_poll(&bar[B_OEMPTY0 + bb], ((u2b >> 1) & 1) ^ 1)) {
+                        tc_fence_after();
+#pragma unroll
+                        for (int s = 0; s < 8; ++s) {  // K-dim = features
+                            const uint64_t a = (s < 4 ? dQ[bb] : dQ2[bb]) + kmaj(s);
+                            mma_ss(tmem + T_ACC + bb * 64, a, dSB[bb] + mnmaj(s), ID_C, s > 0);
+                            mma_ss(tmem + T_DEN + bb * 16, a, dZT[bb] + row1(s), ID_CZ, s > 0);
+                        }
+                        ++u2b;
                         prog = true;
                     }
                 }
                 // ---- group 4: ACC += P' Vw, DEN += P' w  (P' from tensor memory)
-                if (!SO && u4 < u2) {
+                if (!SO && u4 < u2b) {
                     const int bb = u4 & 1;
                     if (mbar_poll(&bar[B_PREADY0 + bb], (u4 >> 1) & 1)) {
                         tc_fence_after();
-                        const uint32_t v_s = sb + bb * STAGE + 2 * TILE;
                         const int n = (u4 == U - 1) ? n_last : C;
-                        const uint32_t w16 = sb + OFF_W16 + (n < C ? ROW1 : 0);
+                        const uint64_t dw = dW[n < C ? 1 : 0];
 #pragma unroll
                         for (int s = 0; s < 8; ++s) {  // K-dim = tokens; P' packs 2 per column
                             const uint32_t pa = tmem + T_A + bb * 128 + s * 8;
-                            mma_ts(tmem + T_ACC + bb * 64, pa, sdesc(v_s + s * 2048, 8192, 1024), ID_C, 1);
-                            mma_ts(tmem + T_DEN + bb * 16, pa, sdesc(w16 + (s >> 2) * 2048 + (s & 3) * 32, 16, 1024),
-                                   ID_CZ, 1);
+                            mma_ts(tmem + T_ACC + bb * 64, pa, dV[bb] + mnmaj(s), ID_C, 1);
+                            mma_ts(tmem + T_DEN + bb * 16, pa, dw + row1(s), ID_CZ, 1);
                         }
                         commit(&bar[B_CDONE0 + bb]);
                         ++u4;
@@ -472,14 +521,16 @@ __global__ void __launch_bounds__(512, 1)
             if (!mbar_wait(&bar[B_CDONE0 + st], ((u >> 1) & 1) ^ 1, ctl, 8)) break;
             uint8_t *q_s = smem + st * STAGE, *k_s = q_s + TILE, *v_s = q_s + 2 * TILE;
             uint8_t *q2 = smem + OFF_DER + st * 2 * TILE, *k2 = q2 + TILE;
+            // Each tile: issue all 8 row loads before any store (the in-place stores would
+            // otherwise keep every load behind the previous row's store).
+            uint4 x[8];
+            if (!SO) {
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const int r = rb * 8 + t;
-                const uint32_t off = swz(r, cc);
-                const __nv_bfloat162 ww = __float2bfloat162_rn(r < n ? sm.pw[n - 1 - r] : 0.f);
-                if (!SO) {
-                    const uint4 x = *reinterpret_cast<const uint4 *>(q_s + off);
-                    uint32_t xq[4] = {x.x, x.y, x.z, x.w}, yq[4];
+                for (int t = 0; t < 8; ++t) x[t] = *reinterpret_cast<const uint4 *>(q_s + swz(rb * 8 + t, cc));
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    const uint32_t off = swz(rb * 8 + t, cc);
+                    uint32_t xq[4] = {x[t].x, x[t].y, x[t].z, x[t].w}, yq[4];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         const __nv_bfloat162 qv = as_b2(xq[c]);
@@ -490,22 +541,28 @@ __global__ void __launch_bounds__(512, 1)
                     *reinterpret_cast<uint4 *>(q_s + off) = make_uint4(xq[0], xq[1], xq[2], xq[3]);
                     *reinterpret_cast<uint4 *>(q2 + off) = make_uint4(yq[0], yq[1], yq[2], yq[3]);
                 }
-                {
-                    const uint4 x = *reinterpret_cast<const uint4 *>(k_s + off);
-                    const uint32_t xk[4] = {x.x, x.y, x.z, x.w};
-                    uint32_t yk[4];
+            }
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) yk[c] = as_u(__hmul2(as_b2(xk[c]), as_b2(xk[c])));
-                    *reinterpret_cast<uint4 *>(k2 + off) = make_uint4(yk[0], yk[1], yk[2], yk[3]);
-                }
-                {
-                    const uint4 x = *reinterpret_cast<const uint4 *>(v_s + off);
-                    const uint32_t xv[4] = {x.x, x.y, x.z, x.w};
-                    uint32_t yv[4];
+            for (int t = 0; t < 8; ++t) x[t] = *reinterpret_cast<const uint4 *>(k_s + swz(rb * 8 + t, cc));
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) yv[c] = as_u(__hmul2(as_b2(xv[c]), ww));
-                    *reinterpret_cast<uint4 *>(v_s + off) = make_uint4(yv[0], yv[1], yv[2], yv[3]);
-                }
+            for (int t = 0; t < 8; ++t) {
+                const uint32_t xk[4] = {x[t].x, x[t].y, x[t].z, x[t].w};
+                uint32_t yk[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) yk[c] = as_u(__hmul2(as_b2(xk[c]), as_b2(xk[c])));
+                *reinterpret_cast<uint4 *>(k2 + swz(rb * 8 + t, cc)) = make_uint4(yk[0], yk[1], yk[2], yk[3]);
+            }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) x[t] = *reinterpret_cast<const uint4 *>(v_s + swz(rb * 8 + t, cc));
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const int r = rb * 8 + t;
+                const __nv_bfloat162 ww = __float2bfloat162_rn(r < n ? sm.pw[n - 1 - r] : 0.f);
+                const uint32_t xv[4] = {x[t].x, x[t].y, x[t].z, x[t].w};
+                uint32_t yv[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) yv[c] = as_u(__hmul2(as_b2(xv[c]), ww));
+                *reinterpret_cast<uint4 *>(v_s + swz(r, cc)) = make_uint4(yv[0], yv[1], yv[2], yv[3]);
             }
             if (u == U - 1 && n < C)  // w row of the partial last chunk
                 *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_W16 + ROW1 + row0(tid)) =
@@ -595,7 +652,8 @@ __global__ void __launch_bounds__(512, 1)
         if (!SO) publish(0);
         fence_proxy_async();
         tc_fence_before();
-        mbar_arrive(&bar[B_SREADY]);
+        mbar_arrive(&bar[B_SREADY0]);
+        mbar_arrive(&bar[B_DSFREE]);
         bool ok = true;
         for (int u = 0; u < U && ok; ++u) {
             const int bb = u & 1;
@@ -609,22 +667,26 @@ __global__ void __launch_bounds__(512, 1)
             tc_fence_after();
             named_bar(2, 128);  // all rows of the previous chunk's output read s0f[bb ^ 1]
             const float decay = sm.pw[n];
-#pragma unroll
-            for (int hcol = 0; hcol < 2; ++hcol) {
+            {
                 float d[32];
-                tmem_ld32(lane_base + T_DS + 32 * hcol, d);
+                tmem_ld32(lane_base + T_DS, d);
 #pragma unroll
-                for (int e = 0; e < 32; ++e) S[32 * hcol + e] = fmaf(decay, S[32 * hcol + e], d[e]);
+                for (int e = 0; e < 32; ++e) S[e] = fmaf(decay, S[e], d[e]);
+                tmem_ld32(lane_base + T_DS + 32, d);
+                const float2 zs = tmem_ld2(lane_base + T_DZS);
+                tc_fence_before();
+                mbar_arrive(&bar[B_DSFREE]);  // dS is in registers: the next chunk's dS GEMMs may start
+#pragma unroll
+                for (int e = 0; e < 32; ++e) S[32 + e] = fmaf(decay, S[32 + e], d[e]);
+                Z = fmaf(decay, Z, zs.x);
+                if (f < D) s0 = fmaf(decay, s0, zs.y);
             }
-            Z = fmaf(decay, Z, tmem_ld1(lane_base + T_DZ));
-            const float ds0 = tmem_ld1(lane_base + T_DS0);
-            if (f < D) s0 = fmaf(decay, s0, ds0);
             const float Z0_in = Z0;
             Z0 = fmaf(decay, Z0, sm.geo[n]);
             if (!SO) publish(bb ^ 1);
             fence_proxy_async();
             tc_fence_before();
-            mbar_arrive(&bar[B_SREADY]);
+            mbar_arrive(&bar[B_SREADY0 + (bb ^ 1)]);
             if (SO) continue;
             // ---- output rows
             if (!mbar_wait(&bar[B_CDONE0 + bb], (u >> 1) & 1, ctl, 14)) {
@@ -636,13 +698,19 @@ __global__ void __launch_bounds__(512, 1)
             const float g = sm.pw[i + 1];
             const float inv = 1.0f / fmaxf(tmem_ld1(lane_base + T_DEN + bb * 16) + g * Z0_in, p.eps);
             TO *yrow = reinterpret_cast<TO *>(p.y.p) + b * p.y.sb + h * p.y.sh + (int64_t)(t0 + i) * p.y.sl;
-            const float *s0in = sm.s0f[bb];
+            const float4 *s0in = reinterpret_cast<const float4 *>(sm.s0f[bb]);
 #pragma unroll
             for (int hcol = 0; hcol < 2; ++hcol) {
                 float acc[32];
                 tmem_ld32(lane_base + T_ACC + bb * 64 + 32 * hcol, acc);
 #pragma unroll
-                for (int e = 0; e < 32; ++e) acc[e] = fmaf(g, s0in[32 * hcol + e], acc[e]) * inv;
+                for (int e4 = 0; e4 < 8; ++e4) {
+                    const float4 sv = s0in[8 * hcol + e4];
+                    acc[4 * e4 + 0] = fmaf(g, sv.x, acc[4 * e4 + 0]) * inv;
+                    acc[4 * e4 + 1] = fmaf(g, sv.y, acc[4 * e4 + 1]) * inv;
+                    acc[4 * e4 + 2] = fmaf(g, sv.z, acc[4 * e4 + 2]) * inv;
+                    acc[4 * e4 + 3] = fmaf(g, sv.w, acc[4 * e4 + 3]) * inv;
+                }
                 if (i < n) store_row32<TO>(yrow + 32 * hcol, acc);
             }
             tc_fence_before();
