@@ -2,45 +2,50 @@
 //
 // Same recurrence as chunked_prime_ssd_core (src/prime_moment_attention/chunked_ssd.py:48-184),
 // evaluated per 128-token chunk (n <= 128 valid tokens) with the moment features
-// psi(q) = [q | q^2/2], phi(k) = [k | k^2] (128 features) written as GEMMs on
-// rescaled operands, so that almost all of the arithmetic runs on tensor cores:
+// psi(q) = [q | q^2/2], phi(k) = [k | k^2] (128 features) written as GEMMs whose
+// operands carry the decay, so that the per-element work is one FMA:
 //
-//   g_i = l^(i+1)   (carry into token i)      w_j = l^(n-1-j)  (token j to chunk end, 0 if j >= n)
-//   Qg  = g . q,  Q2g = g . q^2/2             Vw = w . v                 (rows scaled, bf16)
-//   At  = [Qg | Q2g] [K | K^2]^T  = g_i (q_i.k_j + q_i^2.k_j^2/2)       (M=N=128, K=128)
-//   P'  = l^(i-n+1) + l^-n At     = l^(i-j) (1 + ...) / w_j   for j <= i, else 0
-//   ACC = [Qg | Q2g] [S1; S2]  +  P' Vw   =  g_i carry_i + num_i          (chunked_ssd.py:93,139-148)
-//   DEN = [Qg | Q2g] [Z1; Z2]  +  P' w    =  g_i cden_i  + den_i           (:94,149-153)
-//   y_i = (ACC_i + g_i S0) / max(DEN_i + g_i Z0, eps)                      (:155-157)
-//   dS  = [K | K^2]^T Vw,  dZ = [K | K^2]^T w,  dS0 = Vw^T 1             (:96-111)
+//   g_i = l^(i+1)  (carry into token i)      w_j = l^(n-1-j)  (token j to chunk end; 0 if j >= n)
+//   QQ  = [q | q^2/2]                         KW = [w.k | w.k^2]          (bf16 operands)
+//   At  = QQ KW^T          = w_j a_ij,  a_ij = q_i.k_j + q_i^2.k_j^2/2   (M=N=128, K=128)
+//   P   = l^-n At + l^-(1+j) = l^-(1+j) (1 + a_ij)  for j <= i, else 0   (= l^(i-j)(1+a_ij) / g_i)
+//   ACC = QQ [S1 S2 | Z1 Z2]^T-blocks + P V   -> per row: carry numerator, carry denominator,
+//                                               intra-chunk numerator    (chunked_ssd.py:93-94,139-148)
+//   y_i = (ACC_i + S0) / max(cden_i + sum_j P_ij + Z0, eps / g_i)        (:149-157)
+//   dS  = KW^T V,  dZ = column sums of KW,  dS0 = sum_j w_j v_j           (:96-111)
 //   S   = l^n S + dS   (float32, in registers of the state warpgroup)     (:162-169)
-// The per-element decay mask of the reference becomes one FMA per element;
-// denominators and the S0/Z1/Z2 updates are N=16 GEMMs against one-row tiles.
 // The rescaling keeps every factor inside float32/bf16 range for l >= 0.55
-// (l^-128 < 1e34, l^128 > 1e-34); head-states with a smaller decay run the
+// (l^-128 < 2e33, l^127 > 1e-33); head-states with a smaller decay run the
 // float32 CUDA-core chunk loop (prefill_simt_body.cuh) inside this kernel.
 //
+// The kernel is bound by shared-memory bandwidth (128 B/clk per SM, shared by
+// the tensor core's operand reads and every CUDA-core access), so the layout
+// minimises shared-memory bytes per chunk:
+//   * QQ lives in tensor memory (written by the prep warps with tcgen05.st) and
+//     is the A operand of the score GEMM and of the carry GEMM (no smem reads);
+//   * the decay weights w_j are folded into K (KW, written in place plus a new
+//     K^2 tile); V stays as loaded and is the B operand of dS and P V;
+//   * P is written back over the score accumulator and used from tensor memory;
+//     dS then takes the other half of that accumulator;
+//   * dZ, dS0 and the intra-chunk denominator sum_j P_ij are CUDA-core sums of
+//     values already in registers; the carry denominator is column 64 of an
+//     N=80 carry GEMM whose B operand [S1;S2 | Z] is a 32-byte-swizzled tile.
+// Per chunk: 48 KB of TMA writes, 81 KB of prep traffic, 116 KB of operand reads,
+// 20 KB of state tile writes.
+//
 // Data: q/k/v chunk tiles arrive by TMA (4-D tensor maps over the strided
-// tensors, 128-byte swizzle) into two stages; prep overwrites q by Qg and v by
-// Vw in place and writes Q2g and K^2 to double-buffered tiles.  Accumulators
-// live in tensor memory: At x2 (P' is written back over the consumed At columns
-// and read by the P'-GEMMs from TMEM), ACC x2, dS, DEN x2, and [dZ | dS0] in one
-// 16-column region.  The producer also prefetches the tiles of later chunks
-// into L2, so each stage load finds its data there.  The bf16 state copy
-// [S1; S2] and the one-row [Z1; Z2] tile that feed the carry GEMMs are
-// double-buffered.
+// tensors, 128-byte swizzle) into three stages; the producer also prefetches
+// later chunks into L2.  Tensor memory: At/P/dS x2 (256 columns), QQ x2 (128),
+// ACC (80).
 //
 // Warp roles (512 threads, one CTA per SM):
 //   warp 0        TMA producer
 //   warp 1        MMA issuer (one thread, event driven: issues each chunk's GEMM
-//                 groups as soon as their inputs are ready) and TMEM owner.  The
-//                 state GEMMs of chunk u+1 start as soon as the state warpgroup
-//                 has read dS of chunk u, so the recurrence's critical path is
-//                 one tensor-memory read, the dS GEMMs and one barrier hop.
-//   warps 4-7     prep: Qg, Q2g, K^2, Vw for each chunk
-//   warps 8-11    mask: At -> P' in tensor memory
-//   warps 12-15   state and output: S += dS (thread f owns feature row f), bf16
-//                 state tiles for the next chunk, then y for the chunk's 128 tokens
+//                 groups as soon as their inputs are ready) and TMEM owner
+//   warps 4-7     prep: QQ -> tensor memory, KW and K^2 W tiles, column sums
+//   warps 8-11    mask: At -> P in tensor memory (warps 2-3 take part of quadrants 2-3)
+//   warps 12-15   state: S += dS (thread f owns feature row f), bf16 state tile for the next
+//                 chunk's carry GEMM, then the chunk's output rows (thread i owns token row i)
 // Every wait is bounded by the global timer; on expiry the kernel records a status
 // code in the workspace header, every role stops, and the CTA waits for its
 // in-flight copies and GEMMs before freeing tensor memory.
@@ -55,27 +60,33 @@ namespace tc {
 constexpr int C = TC_CHUNK;   // tokens per chunk
 constexpr int D = 64;
 constexpr int TILE = C * D * 2;           // [128 x 64] bf16 = 16 KiB
-constexpr int STAGE = 3 * TILE;           // q (-> Qg), k, v (-> Vw)
-constexpr int OFF_DER = 2 * STAGE;        // per buffer: Q2g, K^2
-constexpr int OFF_SB = OFF_DER + 4 * TILE;    // bf16 [S1; S2], [128 features][64 values], x2
-constexpr int ROW1 = 4096;                // one-row K-major tile: 2 atoms x 16 rows x 128 B
-constexpr int OFF_ZT = OFF_SB + 2 * TILE;     // [Z1; Z2] row, x2
-constexpr int OFF_W16 = OFF_ZT + 2 * ROW1;    // w row: full chunks, last partial chunk
-constexpr int OFF_ONES = OFF_W16 + 2 * ROW1;  // ones in row 1 (dS0 lands in column 1 of [dZ | dS0])
-constexpr int PREFETCH = 3;               // chunks of L2 prefetch ahead of the stage loads
-constexpr int OFF_SMALL = OFF_ONES + ROW1;
+constexpr int NST = 3;                    // stages of k (-> w.k), v, w.k^2
+constexpr int STAGE = 3 * TILE;
+constexpr int OFF_K = 0, OFF_V = TILE, OFF_K2 = 2 * TILE;
+constexpr int OFF_Q = NST * STAGE;        // two q slots (q is read once, by the prep warps)
+constexpr int OFF_ONES = OFF_Q + 2 * TILE;  // 128 x 64 bf16, column 0 = 1: second N-atom of [V | 1]
+constexpr int OFF_SB = OFF_ONES + TILE;   // [S1;S2 | Z] bf16, K = 128 features x N = 80, 32-byte swizzle
+constexpr int SB_LBO = 4096;              // next 16-column group
+constexpr int SB_SBO = 256;               // next 8-feature group
+constexpr int OFF_SMALL = OFF_SB + 5 * SB_LBO;
+constexpr int PREFETCH = 4;               // chunks of L2 prefetch ahead of the stage loads
 constexpr float LMIN = 0.55f;             // smallest decay the rescaled operands serve
 
 enum {
-    B_FULL0, B_FULL1, B_CDONE0, B_CDONE1, B_PREP0, B_PREP1, B_IFULL0, B_IFULL1, B_PREADY0, B_PREADY1, B_DSFULL,
-    B_DSFREE, B_SREADY0, B_SREADY1, B_OEMPTY0, B_OEMPTY1, B_FINAL, NBAR
+    B_FULL0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_PREP0, B_PREP1, B_PREP2,
+    B_IFULL0, B_IFULL1, B_PREADY0, B_PREADY1, B_DSFULL0, B_DSFULL1, B_DSFREE0, B_DSFREE1,
+    B_QFREE0, B_QFREE1, B_CDONE0, B_CDONE1, B_SREADY0, B_SREADY1, B_OEMPTY, B_QEMPTY0, B_QEMPTY1, B_MLD0, B_MLD1, B_MLD2, B_MLD3,
+    B_FINAL, NBAR
 };
 
 struct Small {
-    uint64_t bar[18];
-    float pw[C + 4];      // l^t, t = 0..C
-    float geo[C + 4];     // sum_{t<n} l^t
-    alignas(16) float s0f[2][D];  // S0 entering the chunk (float32), per chunk parity
+    uint64_t bar[NBAR];
+    float pw[C + 4];              // l^t, t = 0..C
+    float geo[C + 4];             // sum_{t<n} l^t
+    alignas(16) float cinv[C];    // l^-(1+j)
+    alignas(16) float part[NST][4][D];  // per stage and prep warp: column sums of w.v
+    alignas(16) float s0f[3][D];  // S0 entering the chunk, by chunk mod 3
+    float z0f[4];                 // Z0 entering the chunk, by chunk mod 3
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -84,7 +95,8 @@ static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 static_assert(SimtSmem<64, 64>::bytes <= OFF_SMALL, "fallback path fits in the same allocation");
 
 // tensor-memory columns
-constexpr uint32_t T_A = 0, T_ACC = 256, T_DS = 384, T_DEN = 448, T_DZS = 480, T_COLS = 512;
+// At / P / [dS | dZ]: buffer bb at bb * T_AS; At in columns 0..127, then P in 0..63 and [dS | dZ] in 64..143
+constexpr uint32_t T_A = 0, T_AS = 144, T_QQ = 288, T_ACC = 416, T_COLS = 512;
 
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
 
@@ -140,7 +152,7 @@ __device__ __forceinline__ void give_up(const Ctl &ctl, int code) {
     if (ctl.status) atomicCAS(ctl.status, 0, code);
 }
 
-__device__ __noinline__ bool mbar_wait_slow(uint64_t *b, uint32_t parity, const Ctl &ctl, int code) {
+__device__ __forceinline__ bool mbar_wait_slow(uint64_t *b, uint32_t parity, const Ctl &ctl, int code) {
     const unsigned long long t0 = gtimer();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try(b, parity)) return true;
@@ -184,6 +196,11 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
 }
+// Upper fields of a shared-memory matrix descriptor (everything but the start address).
+__host__ __device__ constexpr uint64_t desc_hi(uint32_t lbo, uint32_t sbo, uint32_t swizzle) {
+    return ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) |
+           ((uint64_t)swizzle << 61);
+}
 // Instruction descriptor, kind::f16: bf16 x bf16 -> f32, dense; a_mn/b_mn = operand is MN-major.
 __host__ __device__ constexpr uint32_t idesc(int M, int N, int a_mn, int b_mn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
@@ -209,9 +226,79 @@ __device__ __forceinline__ void commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
                  : "memory");
 }
-// 32 consecutive float32 columns of this thread's TMEM lane.
+// 32 consecutive float32 columns of this thread's TMEM lane (the wait is part of the same
+// statement, so no use of the results can be scheduled before it).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
+    asm volatile(
+        "{\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;\n\t}"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+// Columns taddr..taddr+31 of this thread's lane as two 16-column loads (addresses need only be
+// 16-column aligned), with the wait in the same statement.
+__device__ __forceinline__ void tmem_ld2x16(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "{\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+        "%29, %30, %31}, [%33];\n\t"
+        "tcgen05.wait::ld.sync.aligned;\n\t}"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr), "r"(taddr + 16)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+// One float32 column of this thread's lane, with the wait.
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("{\n\ttcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n\ttcgen05.wait::ld.sync.aligned;\n\t}"
+                 : "=r"(r)
+                 : "r"(taddr)
+                 : "memory");
+    return __uint_as_float(r);
+}
+// Column loads issued only: the values are valid after tmem_wait_ld_regs on the same registers
+// (its "+r" operands keep every use behind the wait).
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
+}
+// 8 consecutive 32-bit columns of this thread's TMEM lane (completion via tmem_wait_st).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
@@ -221,23 +308,32 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr)
         : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
-// One float32 column of this thread's TMEM lane.
-__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
-    uint32_t r;
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-    return __uint_as_float(r);
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
 }
-// Two float32 columns of this thread's TMEM lane.
-__device__ __forceinline__ float2 tmem_ld2(uint32_t taddr) {
-    uint32_t r0, r1;
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(taddr) : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-    return make_float2(__uint_as_float(r0), __uint_as_float(r1));
+// 33 float32 columns (32 consecutive + the one at +64) of this thread's TMEM lane, with the wait.
+__device__ __forceinline__ void tmem_ld33(uint32_t taddr, uint32_t (&r)[32], uint32_t &r64) {
+    asm volatile(
+        "{\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%33];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%32}, [%34];\n\t"
+        "tcgen05.wait::ld.sync.aligned;\n\t}"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r64)
+        : "r"(taddr), "r"(taddr + 64)
+        : "memory");
 }
 // 16 consecutive 32-bit columns of this thread's TMEM lane (completion via tmem_wait_st).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
@@ -259,10 +355,13 @@ __device__ __forceinline__ uint4 pack8(const float *f) {
 }
 __device__ __forceinline__ __nv_bfloat162 as_b2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162 *>(&u); }
 __device__ __forceinline__ uint32_t as_u(__nv_bfloat162 h) { return *reinterpret_cast<uint32_t *>(&h); }
+// bf16 pair -> float pair (exact: bf16 is the upper half of a float32)
+__device__ __forceinline__ float2 bf2f(uint32_t u) {
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+__device__ __forceinline__ uint32_t f2bf(float2 v) { return pack2(v.x, v.y); }
 // byte offset of 16-byte chunk `c` of row `r` in a [rows x 128 B] tile with the 128-byte swizzle
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
-// byte offset of element k of row 0 in a one-row K-major tile (two 64-element atoms of 16 rows)
-__device__ __forceinline__ uint32_t row0(int k) { return (uint32_t)((k >> 6) * 2048 + (k & 63) * 2); }
 
 template <typename TO>
 __device__ __forceinline__ void store_row32(TO *dst, const float *v);
@@ -306,16 +405,24 @@ __global__ void __launch_bounds__(512, 1)
     const int n_last = min(C, p.L - (c_end - 1) * C);
     Ctl ctl{&sm.abort_flag, p.status};
 
-    // ---- set-up: powers, barriers, constant one-row tiles, tensor memory
+    // ---- set-up: powers, barriers, tensor memory
     if (threadIdx.x <= C) sm.pw[threadIdx.x] = (float)pow((double)lam, (double)threadIdx.x);
-    for (int i = threadIdx.x; i < 5 * ROW1 / 16; i += blockDim.x)  // zero ZT x2, W16 x2, ONES
-        reinterpret_cast<uint4 *>(smem + OFF_ZT)[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (threadIdx.x < C) sm.cinv[threadIdx.x] = (float)pow((double)lam, -1.0 - (double)threadIdx.x);
+    for (int i = threadIdx.x; i < TILE / 16; i += blockDim.x) {  // ones tile: row r = i / 8, chunk i % 8
+        const int r = i >> 3, c = i & 7;
+        const uint32_t one = (c == (r & 7)) ? 0x3F80u : 0u;  // element 0 of row r sits in chunk 0 ^ (r & 7)
+        reinterpret_cast<uint4 *>(smem + OFF_ONES)[i] = make_uint4(one, 0u, 0u, 0u);
+    }
     if (threadIdx.x == 0) {
         for (int i = 0; i < NBAR; ++i) {
             uint32_t n = 1;
-            if (i == B_PREP0 || i == B_PREP1 || i == B_PREADY0 || i == B_PREADY1 || i == B_SREADY0 ||
-                i == B_SREADY1 || i == B_DSFREE || i == B_OEMPTY0 || i == B_OEMPTY1)
+            if ((i >= B_PREP0 && i <= B_PREP2) || i == B_PREADY0 || i == B_PREADY1 || i == B_DSFREE0 ||
+                i == B_DSFREE1 || i == B_SREADY0 || i == B_SREADY1 || i == B_OEMPTY || i == B_QEMPTY0 ||
+                i == B_QEMPTY1)
                 n = 128;
+            if (i >= B_EMPTY0 && i <= B_EMPTY2) n = 2 + 128;  // two GEMM-group commits + the state warpgroup
+            if (i == B_PREADY0 || i == B_PREADY1) n = 128 + 64;  // mask warps 8-11 + helpers 2-3
+            if (i >= B_MLD0 && i <= B_MLD3) n = 32;              // one mask warp
             mbar_init(&sm.bar[i], n);
         }
         sm.abort_flag = 0;
@@ -330,6 +437,7 @@ __global__ void __launch_bounds__(512, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    fence_proxy_async();  // the ones tile is read by the tensor core
     if (threadIdx.x == 0) {
         float g = 0.f;
         for (int j = 0; j <= C; ++j) {
@@ -337,12 +445,6 @@ __global__ void __launch_bounds__(512, 1)
             if (j < C) g += sm.pw[j];
         }
     }
-    if (threadIdx.x < C) {  // w row for full chunks, and the ones row
-        const int j = threadIdx.x;
-        *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_W16 + row0(j)) = __float2bfloat16_rn(sm.pw[C - 1 - j]);
-        *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_ONES + 128 + row0(j)) = __float2bfloat16_rn(1.0f);
-    }
-    fence_proxy_async();
     __syncthreads();
     const uint32_t tmem = sm.tmem_base;
     uint64_t *bar = sm.bar;
@@ -351,153 +453,121 @@ __global__ void __launch_bounds__(512, 1)
         // ============================== TMA producer
         if (lane == 0) {
             int issued = 0, fetched = 0;
-            for (int u = 0; u < U; ++u) {
+            for (int u = 0, s = 0; u < U; ++u, s = (s == NST - 1) ? 0 : s + 1) {
                 for (; fetched < U && fetched <= u + PREFETCH; ++fetched) {
                     const int tf = (c_begin + fetched) * C;
                     if (!SO) tma_prefetch_l2(&tq, 0, tf, h, b);
                     tma_prefetch_l2(&tk, 0, tf, h, b);
                     tma_prefetch_l2(&tv, 0, tf, h, b);
                 }
-                const int st = u & 1;
-                if (!mbar_wait(&bar[B_CDONE0 + st], ((u >> 1) & 1) ^ 1, ctl, 1)) break;
+                if (!mbar_wait(&bar[B_EMPTY0 + s], ((u / NST) & 1) ^ 1, ctl, 1)) break;
+                if (!SO && !mbar_wait(&bar[B_QEMPTY0 + (u & 1)], ((u >> 1) & 1) ^ 1, ctl, 3)) break;
                 const int t0 = (c_begin + u) * C;
-                uint8_t *base = smem + st * STAGE;
-                mbar_expect_tx(&bar[B_FULL0 + st], SO ? 2 * TILE : 3 * TILE);
-                if (!SO) tma_load(base, &tq, &bar[B_FULL0 + st], 0, t0, h, b);
-                tma_load(base + TILE, &tk, &bar[B_FULL0 + st], 0, t0, h, b);
-                tma_load(base + 2 * TILE, &tv, &bar[B_FULL0 + st], 0, t0, h, b);
+                uint8_t *base = smem + s * STAGE;
+                mbar_expect_tx(&bar[B_FULL0 + s], SO ? 2 * TILE : 3 * TILE);
+                if (!SO) tma_load(smem + OFF_Q + (u & 1) * TILE, &tq, &bar[B_FULL0 + s], 0, t0, h, b);
+                tma_load(base + OFF_K, &tk, &bar[B_FULL0 + s], 0, t0, h, b);
+                tma_load(base + OFF_V, &tv, &bar[B_FULL0 + s], 0, t0, h, b);
                 issued = u + 1;
             }
-            // never leave with copies in flight: the last (up to) two stages must have landed
-            for (int u = max(0, issued - 2); u < issued; ++u) {
+            // never leave with copies in flight: the last (up to) NST stages must have landed
+            for (int u = max(0, issued - NST); u < issued; ++u) {
                 const unsigned long long t0 = gtimer();
-                while (!mbar_try(&bar[B_FULL0 + (u & 1)], (u >> 1) & 1) && gtimer() - t0 < WAIT_NS) {
+                while (!mbar_try(&bar[B_FULL0 + u % NST], (u / NST) & 1) && gtimer() - t0 < WAIT_NS) {
                 }
             }
         }
     } else if (warp == 1) {
         // ============================== MMA issuer
         if (lane == 0) {
-            constexpr uint32_t ID_A = idesc(128, 128, 0, 0);  // [Qg|Q2g][K|K2]^T
-            constexpr uint32_t ID_DS = idesc(128, 64, 1, 1);  // [K|K2]^T Vw
-            constexpr uint32_t ID_DZ = idesc(128, 16, 1, 0);  // [K|K2]^T w, [Vw|.]^T 1
-            constexpr uint32_t ID_C = idesc(128, 64, 0, 1);   // [Qg|Q2g][S1;S2], P' Vw
-            constexpr uint32_t ID_CZ = idesc(128, 16, 0, 0);  // [Qg|Q2g][Z1;Z2], P' w
-            // Every operand descriptor is built once; a k-step only adds a constant to its start
-            // address field (the issue loop is what bounds a single-thread MMA issuer).
-            // (pairs per buffer; a ternary select keeps them in registers)
-            struct D2 {
-                uint64_t v0, v1;
-                __device__ __forceinline__ uint64_t operator[](int b) const { return b ? v1 : v0; }
+            constexpr uint32_t ID_A = idesc(128, 128, 0, 0);   // QQ (tmem) KW^T
+            constexpr uint32_t ID_DS = idesc(128, 80, 1, 1);   // KW^T [V | 1]
+            constexpr uint32_t ID_CY = idesc(128, 80, 0, 1);   // QQ (tmem) [S1;S2 | Z]
+            constexpr uint32_t ID_PV = idesc(128, 80, 0, 1);   // P (tmem) [V | 1]
+            // Operand descriptors: a compile-time upper word (strides, version, swizzle) or'ed with the
+            // start-address field, which is the smem base (16-byte units) plus constant offsets; only
+            // that one 32-bit base stays live across the loop.
+            const uint32_t a0 = sb >> 4;  // the whole allocation sits below 256 KiB: no field overflow
+            constexpr uint64_t HI_KMAJ = desc_hi(16, 1024, 2), HI_KMN = desc_hi(OFF_K2 - OFF_K, 1024, 2),
+                               HI_SB = desc_hi(SB_LBO, SB_SBO, 6);
+            auto dsc = [&](uint32_t byte_off, uint64_t hi) { return (uint64_t)(a0 + (byte_off >> 4)) | hi; };
+            // [V | 1] of stage s: the second N-atom is the shared ones tile, LBO = its distance from V
+            auto dvo = [&](int s) {
+                const uint32_t off = (uint32_t)(s * STAGE + OFF_V);
+                return dsc(off, desc_hi(OFF_ONES - off, 1024, 2));
             };
-            auto mk = [&](auto f) { return D2{f(0), f(1)}; };
-            const uint32_t st1 = STAGE, der1 = 2 * TILE;
-            const D2 dQ = mk([&](int b) { return sdesc(sb + b * st1, 16, 1024); });
-            const D2 dQ2 = mk([&](int b) { return sdesc(sb + OFF_DER + b * der1, 16, 1024); });
-            const D2 dK = mk([&](int b) { return sdesc(sb + b * st1 + TILE, 16, 1024); });
-            const D2 dK2 = mk([&](int b) { return sdesc(sb + OFF_DER + b * der1 + TILE, 16, 1024); });
-            // [K | K2] and [Vw | K2] as MN-major A operands: two 64-row atoms, LBO = distance to K2
-            const D2 dKmn = mk([&](int b) {
-                return sdesc(sb + b * st1 + TILE, (OFF_DER + b * der1 + TILE) - (b * st1 + TILE), 1024);
-            });
-            const D2 dVmn = mk([&](int b) {
-                return sdesc(sb + b * st1 + 2 * TILE, (OFF_DER + b * der1 + TILE) - (b * st1 + 2 * TILE), 1024);
-            });
-            const D2 dV = mk([&](int b) { return sdesc(sb + b * st1 + 2 * TILE, 8192, 1024); });
-            const D2 dSB = mk([&](int b) { return sdesc(sb + OFF_SB + b * TILE, 8192, 1024); });
-            const D2 dZT = mk([&](int b) { return sdesc(sb + OFF_ZT + b * ROW1, 16, 1024); });
-            const D2 dW = mk([&](int b) { return sdesc(sb + OFF_W16 + b * ROW1, 16, 1024); });
-            const uint64_t dONES = sdesc(sb + OFF_ONES, 16, 1024);
-            // descriptor start-address steps (16-byte units) of k-step s
-            auto kmaj = [](int s) { return (uint64_t)((s & 3) * 2); };                  // +32 B in a 128 B row
-            auto mnmaj = [](int s) { return (uint64_t)(s * 128); };                     // +16 rows of 128 B
-            auto row1 = [](int s) { return (uint64_t)((s >> 2) * 128 + (s & 3) * 2); };  // one-row K-major tile
-            int u1 = 0, u2a = 0, u2b = 0, u4 = 0;
-            const int U2b = SO ? 0 : U;
-            unsigned long long last = gtimer();
-            while (u2a < U || u2b < U2b || (!SO && u4 < U)) {
-                if (*ctl.abort_flag) break;
-                bool prog = false;
-                // ---- group 1: At = [Qg|Q2g][K|K2]^T into At[u1 & 1]
-                if (!SO && u1 < U) {
-                    const int bb = u1 & 1;
-                    if (mbar_poll(&bar[B_PREP0 + bb], (u1 >> 1) & 1) &&
-                        mbar_poll(&bar[B_CDONE0 + bb], ((u1 >> 1) & 1) ^ 1)) {
-                        tc_fence_after();
+            auto kmaj = [](int k) { return (uint64_t)((k & 3) * 2); };  // +32 B in a 128 B row
+            auto mnmaj = [](int k) { return (uint64_t)(k * 128); };     // +16 rows of 128 B
+            // Static issue order with blocking waits: G1(0), then per chunk u
+            //   [dS(u)], [score(u+1)], [carry(u)], [P V(u)]
+            // so that the tensor pipe always has the next group queued: the score GEMM of u+1 needs
+            // P V(u-1) complete (its accumulator columns), which finished while dS(u) ran; the carry
+            // GEMM of u needs the outputs of u-1 read, which happens while dS(u) and score(u+1) run.
+            // Every wait below depends only on groups issued earlier, so the order cannot deadlock.
+            auto g1 = [&](int u) -> bool {  // At = QQ KW^T into At[u & 1]
+                const int bb = u & 1, st = u % NST, ph = (u >> 1) & 1;
+                if (!mbar_wait(&bar[B_PREP0 + st], (u / NST) & 1, ctl, 20) ||
+                    !mbar_wait(&bar[B_CDONE0 + bb], ph ^ 1, ctl, 21) || !mbar_wait(&bar[B_DSFREE0 + bb], ph ^ 1, ctl, 22))
+                    return false;
+                tc_fence_after();
 #pragma unroll
-                        for (int s = 0; s < 8; ++s)
-                            mma_ss(tmem + T_A + bb * 128, (s < 4 ? dQ[bb] : dQ2[bb]) + kmaj(s),
-                                   (s < 4 ? dK[bb] : dK2[bb]) + kmaj(s), ID_A, s > 0);
-                        commit(&bar[B_IFULL0 + bb]);
-                        ++u1;
-                        prog = true;
-                    }
+                for (int k = 0; k < 8; ++k)
+                    mma_ts(tmem + T_A + bb * T_AS, tmem + T_QQ + bb * 64 + k * 8,
+                           dsc(st * STAGE + (k < 4 ? OFF_K : OFF_K2), HI_KMAJ) + kmaj(k), ID_A, k > 0);
+                commit(&bar[B_IFULL0 + bb]);
+                return true;
+            };
+            auto g2a = [&](int u) -> bool {  // [dS | dZ] = KW^T [V | 1], into the At columns P does not use
+                const int bb = u & 1, st = u % NST, ph = (u >> 1) & 1;
+                if (SO) {
+                    if (!mbar_wait(&bar[B_PREP0 + st], (u / NST) & 1, ctl, 23) ||
+                        !mbar_wait(&bar[B_DSFREE0 + bb], ph ^ 1, ctl, 22))
+                        return false;
+                } else if (!mbar_wait(&bar[B_PREADY0 + bb], ph, ctl, 24)) {
+                    return false;
                 }
-                // ---- group 2a: dS = [K|K2]^T Vw, [dZ | dS0] of chunk u2a.  Needs the state warpgroup
-                // to have read dS of the previous chunk, and (for the bf16 state buffers' reuse)
-                // the previous chunk's carry GEMMs issued before it.
-                if (u2a < U && (SO || u2a <= u2b)) {
-                    const int bb = u2a & 1;
-                    if (mbar_poll(&bar[B_PREP0 + bb], (u2a >> 1) & 1) && mbar_poll(&bar[B_DSFREE], u2a & 1)) {
-                        tc_fence_after();
-                        const int n = (u2a == U - 1) ? n_last : C;
-                        const uint64_t dw = dW[n < C ? 1 : 0];
+                tc_fence_after();
 #pragma unroll
-                        for (int s = 0; s < 8; ++s) {  // K-dim = tokens, 16 rows = 2048 B per step
-                            mma_ss(tmem + T_DS, dKmn[bb] + mnmaj(s), dV[bb] + mnmaj(s), ID_DS, s > 0);
-                            mma_ss(tmem + T_DZS, dKmn[bb] + mnmaj(s), dw + row1(s), ID_DZ, s > 0);
-                        }
-#pragma unroll
-                        for (int s = 0; s < 8; ++s)  // column 1 of [dZ | dS0]: ones sit in row 1 of their tile
-                            mma_ss(tmem + T_DZS, dVmn[bb] + mnmaj(s), dONES + row1(s), ID_DZ, 1);
-                        commit(&bar[B_DSFULL]);
-                        if (SO) commit(&bar[B_CDONE0 + bb]);
-                        ++u2a;
-                        prog = true;
-                    }
+                for (int k = 0; k < 8; ++k)  // K-dim = tokens, 16 rows = 2048 B per step
+                    mma_ss(tmem + T_A + bb * T_AS + 64, dsc(st * STAGE + OFF_K, HI_KMN) + mnmaj(k),
+                           dvo(st) + mnmaj(k), ID_DS, k > 0);
+                commit(&bar[B_DSFULL0 + bb]);
+                commit(&bar[B_EMPTY0 + st]);
+                if (SO) {  // no carry / P V groups: they would make these arrivals
+                    commit(&bar[B_QFREE0 + bb]);
+                    commit(&bar[B_EMPTY0 + st]);
                 }
-                // ---- group 2b: carry GEMMs of chunk u2b with the state entering it
-                if (!SO && u2b < u2a && u2b < u1) {
-                    const int bb = u2b & 1;
-                    if (mbar_poll(&bar[B_SREADY0 + bb], (u2b >> 1) & 1) &&
-                        mbar_poll(&bar[B_OEMPTY0 + bb], ((u2b >> 1) & 1) ^ 1)) {
-                        tc_fence_after();
+                return true;
+            };
+            auto g2b = [&](int u) -> bool {  // carry GEMM with the state entering chunk u: ACC = QQ [S1;S2 | Z]
+                const int bb = u & 1;
+                if (!mbar_wait(&bar[B_SREADY0 + bb], (u >> 1) & 1, ctl, 25) ||
+                    !mbar_wait(&bar[B_OEMPTY], (u & 1) ^ 1, ctl, 26))
+                    return false;
+                tc_fence_after();
 #pragma unroll
-                        for (int s = 0; s < 8; ++s) {  // K-dim = features
-                            const uint64_t a = (s < 4 ? dQ[bb] : dQ2[bb]) + kmaj(s);
-                            mma_ss(tmem + T_ACC + bb * 64, a, dSB[bb] + mnmaj(s), ID_C, s > 0);
-                            mma_ss(tmem + T_DEN + bb * 16, a, dZT[bb] + row1(s), ID_CZ, s > 0);
-                        }
-                        ++u2b;
-                        prog = true;
-                    }
-                }
-                // ---- group 4: ACC += P' Vw, DEN += P' w  (P' from tensor memory)
-                if (!SO && u4 < u2b) {
-                    const int bb = u4 & 1;
-                    if (mbar_poll(&bar[B_PREADY0 + bb], (u4 >> 1) & 1)) {
-                        tc_fence_after();
-                        const int n = (u4 == U - 1) ? n_last : C;
-                        const uint64_t dw = dW[n < C ? 1 : 0];
+                for (int k = 0; k < 8; ++k)  // K-dim = features, 16 per step = 2 groups of 256 B
+                    mma_ts(tmem + T_ACC, tmem + T_QQ + bb * 64 + k * 8, dsc(OFF_SB + k * 512, HI_SB), ID_CY, k > 0);
+                commit(&bar[B_QFREE0 + bb]);
+                return true;
+            };
+            auto g4 = [&](int u) {  // ACC += P [V | 1] (P from tensor memory; column 64 collects the row sums)
+                const int bb = u & 1, st = u % NST;
 #pragma unroll
-                        for (int s = 0; s < 8; ++s) {  // K-dim = tokens; P' packs 2 per column
-                            const uint32_t pa = tmem + T_A + bb * 128 + s * 8;
-                            mma_ts(tmem + T_ACC + bb * 64, pa, dV[bb] + mnmaj(s), ID_C, 1);
-                            mma_ts(tmem + T_DEN + bb * 16, pa, dw + row1(s), ID_CZ, 1);
-                        }
-                        commit(&bar[B_CDONE0 + bb]);
-                        ++u4;
-                        prog = true;
-                    }
-                }
-                if (prog) {
-                    last = gtimer();
-                } else {
-                    if (gtimer() - last > WAIT_NS) {
-                        give_up(ctl, 2);
-                        break;
-                    }
-                    __nanosleep(32);
+                for (int k = 0; k < 8; ++k)  // K-dim = tokens; P packs 2 per column
+                    mma_ts(tmem + T_ACC, tmem + T_A + bb * T_AS + k * 8, dvo(st) + mnmaj(k), ID_PV, 1);
+                commit(&bar[B_CDONE0 + bb]);
+                commit(&bar[B_EMPTY0 + st]);
+            };
+            if (SO) {
+                for (int u = 0; u < U; ++u)
+                    if (!g2a(u)) break;
+            } else if (g1(0)) {
+                for (int u = 0; u < U; ++u) {
+                    if (!g2a(u)) break;
+                    if (u + 1 < U && !g1(u + 1)) break;
+                    if (!g2b(u)) break;
+                    g4(u);  // its P was waited for by dS(u)
                 }
             }
             // every GEMM issued must be complete before tensor memory is released
@@ -507,115 +577,199 @@ __global__ void __launch_bounds__(512, 1)
             }
         }
     } else if (warp >= 4 && warp < 8) {
-        // ============================== prep: Qg (in place), Q2g, K^2 (new tiles), Vw (in place)
+        // ============================== prep: QQ -> tensor memory, KW / K2W tiles, column sums of w.v
         const int tid = threadIdx.x - 128;
-        const int cc = tid & 7, rb = tid >> 3;  // one 16-byte column chunk of 8 rows
-        __nv_bfloat162 gq[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) gq[t] = __float2bfloat162_rn(sm.pw[rb * 8 + t + 1]);
-        const __nv_bfloat162 half2 = __float2bfloat162_rn(0.5f);
-        for (int u = 0; u < U; ++u) {
-            const int st = u & 1;
+        const int wp = warp - 4;
+        const int cc = lane & 7;  // K/V tiles: the thread's 16-byte column chunk
+        const int q_base = wp == 0 ? 0 : (wp == 1 ? 12 : (wp == 2 ? 20 : 28));  // first row quad of the warp
+        const int nq_pass = wp == 0 ? 3 : (wp == 3 ? 1 : 2);                    // quads per thread
+        const uint32_t lane_base = tmem + ((uint32_t)(wp * 32) << 16);
+        for (int u = 0, s = 0; u < U; ++u, s = (s == NST - 1) ? 0 : s + 1) {
+            const int bb = u & 1;
             const int n = (u == U - 1) ? n_last : C;
-            if (!mbar_wait(&bar[B_FULL0 + st], (u >> 1) & 1, ctl, 7)) break;
-            if (!mbar_wait(&bar[B_CDONE0 + st], ((u >> 1) & 1) ^ 1, ctl, 8)) break;
-            uint8_t *q_s = smem + st * STAGE, *k_s = q_s + TILE, *v_s = q_s + 2 * TILE;
-            uint8_t *q2 = smem + OFF_DER + st * 2 * TILE, *k2 = q2 + TILE;
-            // Each tile: issue all 8 row loads before any store (the in-place stores would
-            // otherwise keep every load behind the previous row's store).
-            uint4 x[8];
+            if (!mbar_wait(&bar[B_FULL0 + s], (u / NST) & 1, ctl, 7)) break;
+            uint8_t *k_s = smem + s * STAGE + OFF_K, *v_s = smem + s * STAGE + OFF_V, *k2_s = smem + s * STAGE + OFF_K2;
+            uint4 xq[8];  // row tid of q, kept in registers until its tensor-memory buffer is free
             if (!SO) {
+                const uint8_t *q_s = smem + OFF_Q + bb * TILE;
 #pragma unroll
-                for (int t = 0; t < 8; ++t) x[t] = *reinterpret_cast<const uint4 *>(q_s + swz(rb * 8 + t, cc));
+                for (int c = 0; c < 8; ++c) xq[c] = *reinterpret_cast<const uint4 *>(q_s + swz(tid, c));
+                mbar_arrive(&bar[B_QEMPTY0 + bb]);  // the q slot may be reloaded
+            }
+            // KW = w.k in place and K2W = KW.k (packed bf16 products), and the column sums of w.v
+            // (float32).  Items of 4 rows x one 16-byte column chunk; the row quads are split
+            // unevenly over the warps (12/8/8/4 of 32) so that sub-partition 3, which also runs the
+            // longest mask rows, gets the least.
+            float2 s0p[4];
 #pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    const uint32_t off = swz(rb * 8 + t, cc);
-                    uint32_t xq[4] = {x[t].x, x[t].y, x[t].z, x[t].w}, yq[4];
+            for (int c = 0; c < 4; ++c) s0p[c] = make_float2(0.f, 0.f);
+#pragma unroll 1
+            for (int m = 0; m < nq_pass; ++m) {
+                const int r0 = (q_base + (lane >> 3) + 4 * m) * 4;
+                float wr[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) wr[t] = r0 + t < n ? sm.pw[n - 1 - (r0 + t)] : 0.f;
+                uint4 x[4], y[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    x[t] = *reinterpret_cast<const uint4 *>(k_s + swz(r0 + t, cc));
+                    y[t] = *reinterpret_cast<const uint4 *>(v_s + swz(r0 + t, cc));
+                }
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const uint32_t e4[4] = {x[t].x, x[t].y, x[t].z, x[t].w};
+                    const uint32_t v4[4] = {y[t].x, y[t].y, y[t].z, y[t].w};
+                    const float2 w2 = make_float2(wr[t], wr[t]);
+                    const __nv_bfloat162 wb = __float2bfloat162_rn(wr[t]);
+                    uint32_t o1[4], o2[4];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        const __nv_bfloat162 qv = as_b2(xq[c]);
-                        const __nv_bfloat162 qg = __hmul2(qv, gq[t]);
-                        yq[c] = as_u(__hmul2(qg, __hmul2(qv, half2)));
-                        xq[c] = as_u(qg);
+                        const __nv_bfloat162 kv = as_b2(e4[c]);
+                        const __nv_bfloat162 kw = __hmul2(kv, wb);
+                        o1[c] = as_u(kw);
+                        o2[c] = as_u(__hmul2(kw, kv));
+                        s0p[c] = __ffma2_rn(bf2f(v4[c]), w2, s0p[c]);
                     }
-                    *reinterpret_cast<uint4 *>(q_s + off) = make_uint4(xq[0], xq[1], xq[2], xq[3]);
-                    *reinterpret_cast<uint4 *>(q2 + off) = make_uint4(yq[0], yq[1], yq[2], yq[3]);
+                    const uint32_t off = swz(r0 + t, cc);
+                    *reinterpret_cast<uint4 *>(k_s + off) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+                    *reinterpret_cast<uint4 *>(k2_s + off) = make_uint4(o2[0], o2[1], o2[2], o2[3]);
                 }
             }
+            // lanes cc, cc+8, cc+16, cc+24 of this warp share the column chunk
 #pragma unroll
-            for (int t = 0; t < 8; ++t) x[t] = *reinterpret_cast<const uint4 *>(k_s + swz(rb * 8 + t, cc));
+            for (int m = 8; m <= 16; m <<= 1) {
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const uint32_t xk[4] = {x[t].x, x[t].y, x[t].z, x[t].w};
-                uint32_t yk[4];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) yk[c] = as_u(__hmul2(as_b2(xk[c]), as_b2(xk[c])));
-                *reinterpret_cast<uint4 *>(k2 + swz(rb * 8 + t, cc)) = make_uint4(yk[0], yk[1], yk[2], yk[3]);
+                for (int c = 0; c < 4; ++c)
+                    s0p[c] = __fadd2_rn(s0p[c], make_float2(__shfl_xor_sync(0xffffffffu, s0p[c].x, m),
+                                                            __shfl_xor_sync(0xffffffffu, s0p[c].y, m)));
             }
-#pragma unroll
-            for (int t = 0; t < 8; ++t) x[t] = *reinterpret_cast<const uint4 *>(v_s + swz(rb * 8 + t, cc));
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const int r = rb * 8 + t;
-                const __nv_bfloat162 ww = __float2bfloat162_rn(r < n ? sm.pw[n - 1 - r] : 0.f);
-                const uint32_t xv[4] = {x[t].x, x[t].y, x[t].z, x[t].w};
-                uint32_t yv[4];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) yv[c] = as_u(__hmul2(as_b2(xv[c]), ww));
-                *reinterpret_cast<uint4 *>(v_s + swz(r, cc)) = make_uint4(yv[0], yv[1], yv[2], yv[3]);
+            if (lane < 8) {
+                float4 *pp = reinterpret_cast<float4 *>(sm.part[s][wp]) + cc * 2;
+                pp[0] = make_float4(s0p[0].x, s0p[0].y, s0p[1].x, s0p[1].y);
+                pp[1] = make_float4(s0p[2].x, s0p[2].y, s0p[3].x, s0p[3].y);
             }
-            if (u == U - 1 && n < C)  // w row of the partial last chunk
-                *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_W16 + ROW1 + row0(tid)) =
-                    __float2bfloat16_rn(tid < n ? sm.pw[n - 1 - tid] : 0.f);
-            fence_proxy_async();
-            mbar_arrive(&bar[B_PREP0 + st]);
-        }
-    } else if (warp >= 8 && warp < 12) {
-        // ============================== mask: At -> P' = l^(i-n+1) + l^-n At (j <= i), in tensor memory
-        if (!SO) {
-            const int wq = warp - 8;
-            const int i = wq * 32 + lane;
-            const uint32_t lane_base = tmem + ((uint32_t)(wq * 32) << 16);
-            for (int u = 0; u < U; ++u) {
-                const int bb = u & 1;
-                const int n = (u == U - 1) ? n_last : C;
-                const float cn = 1.0f / sm.pw[n];        // l^-n
-                const float ri = sm.pw[i + 1] * cn;      // l^(i+1-n)
-                if (!mbar_wait(&bar[B_IFULL0 + bb], (u >> 1) & 1, ctl, 9)) break;
-                tc_fence_after();
-                const uint32_t abase = lane_base + T_A + bb * 128;
-#pragma unroll 1
-                for (int g = 0; g < 4; ++g) {
-                    uint32_t pk[16];
-                    if (g > wq) {  // columns above the diagonal for every row of this warp
+            // QQ row tid: [q | q^2/2], 2 bf16 per tensor-memory column, once the carry GEMM of chunk
+            // u-2 has finished reading this buffer
+            if (!mbar_wait(&bar[B_QFREE0 + bb], ((u >> 1) & 1) ^ 1, ctl, 8)) break;
+            if (!SO) {
+                const __nv_bfloat162 half2 = __float2bfloat162_rn(0.5f);
+                uint32_t r[16];
 #pragma unroll
-                        for (int c = 0; c < 16; ++c) pk[c] = 0u;
-                    } else {
-                        float a[32];
-                        tmem_ld32(abase + 32 * g, a);
-                        if (g < wq) {
+                for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
-                            for (int c = 0; c < 16; ++c)
-                                pk[c] = pack2(fmaf(cn, a[2 * c], ri), fmaf(cn, a[2 * c + 1], ri));
-                        } else {
+                    for (int c = 0; c < 4; ++c) {
+                        const uint4 v = xq[4 * hh + c];
+                        r[4 * c + 0] = v.x; r[4 * c + 1] = v.y; r[4 * c + 2] = v.z; r[4 * c + 3] = v.w;
+                    }
+                    tmem_st16(lane_base + T_QQ + bb * 64 + 16 * hh, r);
+                }
 #pragma unroll
-                            for (int c = 0; c < 16; ++c)
-                                pk[c] = pack2(2 * c <= lane ? fmaf(cn, a[2 * c], ri) : 0.f,
-                                              2 * c + 1 <= lane ? fmaf(cn, a[2 * c + 1], ri) : 0.f);
+                for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint4 v = xq[4 * hh + c];
+                        const uint32_t e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const __nv_bfloat162 qv = as_b2(e[t]);
+                            r[4 * c + t] = as_u(__hmul2(qv, __hmul2(qv, half2)));  // q*(q/2): one rounding
                         }
                     }
-                    // P' of columns 32g..32g+31 -> columns 16g..16g+15, whose At values were already read
-                    tmem_st16(abase + 16 * g, pk);
+                    tmem_st16(lane_base + T_QQ + bb * 64 + 32 + 16 * hh, r);
+                }
+                tmem_wait_st();
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            mbar_arrive(&bar[B_PREP0 + s]);
+        }
+    } else if ((warp >= 8 && warp < 12) || warp == 2 || warp == 3) {
+        // ============================== mask: At -> P
+        // TMEM lane quadrant q = warp % 4 holds rows 32q..32q+31, whose P has 2q+2 nonzero 16-column
+        // blocks.  Warps 8-11 own the quadrants; warps 2 and 3 take the upper half of the blocks of
+        // quadrants 2 and 3.  P of block b (At columns 16b..16b+15) goes to columns 8b..8b+7, which
+        // only this quadrant reads: a helper stores after the owner has its At blocks in registers.
+        if (!SO) {
+            const int wq = warp & 3;
+            const bool helper = warp < 4;
+            const int i = wq * 32 + lane;
+            const uint32_t lane_base = tmem + ((uint32_t)(wq * 32) << 16);
+            const int nq = 2 * wq + 2;                                   // nonzero blocks of the quadrant
+            const int split = wq == 2 ? 3 : (wq == 3 ? 4 : nq);          // first block of the helper
+            const int b0 = helper ? split : 0, nb = helper ? nq - split : split;
+            const int zero_from = (wq == 2) ? (helper ? 48 : 64) : (wq < 2 ? 16 * wq + 16 : 64);
+            uint64_t *mld = &bar[B_MLD0 + 2 * (wq - 2)];                 // quadrants 2, 3: [chunk parity]
+            auto mask = [&](int u) -> bool {
+                const int bb = u & 1;
+                const int n = (u == U - 1) ? n_last : C;
+                const float cn = 1.0f / sm.pw[n];  // l^-n
+                const float2 cn2 = make_float2(cn, cn);
+                if (!mbar_wait(&bar[B_IFULL0 + bb], (u >> 1) & 1, ctl, 9)) return false;
+                tc_fence_after();
+                const uint32_t abase = lane_base + T_A + bb * T_AS;
+                uint32_t ra[4][16];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < nb) tmem_ld16_issue(abase + 16 * (b0 + j), ra[j]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < nb) tmem_wait_ld_regs(ra[j]);
+                if (split < nq) {
+                    if (!helper) {
+                        tc_fence_before();
+                        mbar_arrive(&mld[bb]);  // this warp's At columns are in registers
+                    } else if (!mbar_wait(&mld[bb], (u >> 1) & 1, ctl, 10)) {
+                        return false;
+                    } else {
+                        tc_fence_after();
+                    }
+                }
+                if (zero_from < 64) {  // P columns right of the diagonal block: zero for every row here
+                    uint32_t z[16];
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) z[c] = 0u;
+#pragma unroll 1
+                    for (int c0 = zero_from; c0 < 64; c0 += 16) tmem_st16(abase + c0, z);
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (j < nb) {
+                        const int bk = b0 + j;
+                        const float4 *cv = reinterpret_cast<const float4 *>(sm.cinv + 16 * bk);
+                        const int lim = lane - 16 * (bk - 2 * wq);  // column 16bk + c belongs to row i iff c <= lim
+                        uint32_t pk[8];
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; ++c4) {
+                            const float4 cj = cv[c4];
+                            float2 lo = __ffma2_rn(
+                                cn2, make_float2(__uint_as_float(ra[j][4 * c4]), __uint_as_float(ra[j][4 * c4 + 1])),
+                                make_float2(cj.x, cj.y));
+                            float2 hi = __ffma2_rn(
+                                cn2,
+                                make_float2(__uint_as_float(ra[j][4 * c4 + 2]), __uint_as_float(ra[j][4 * c4 + 3])),
+                                make_float2(cj.z, cj.w));
+                            lo.x = 4 * c4 <= lim ? lo.x : 0.f;
+                            lo.y = 4 * c4 + 1 <= lim ? lo.y : 0.f;
+                            hi.x = 4 * c4 + 2 <= lim ? hi.x : 0.f;
+                            hi.y = 4 * c4 + 3 <= lim ? hi.y : 0.f;
+                            pk[2 * c4] = f2bf(lo);
+                            pk[2 * c4 + 1] = f2bf(hi);
+                        }
+                        tmem_st8(abase + 8 * bk, pk);
+                    }
                 }
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&bar[B_PREADY0 + bb]);
-            }
+                return true;
+            };
+            for (int u = 0; u < U; ++u)
+                if (!mask(u)) break;
         }
     } else if (warp >= 12) {
-        // ============================== state update + output rows
+        // ============================== state: S += dS, bf16 state tile for the carry GEMM
         const int wq = warp - 12;
-        const int f = wq * 32 + lane;  // feature row for the state, token row for the output
+        const int f = wq * 32 + lane;  // feature row: f < 64 -> S1 row f, else S2 row f - 64
         const uint32_t lane_base = tmem + ((uint32_t)(wq * 32) << 16);
         float S[D];
         float Z, s0 = 0.f, Z0;
@@ -642,79 +796,114 @@ __global__ void __launch_bounds__(512, 1)
             Z = 0.f;
             Z0 = 0.f;
         }
-        auto publish = [&](int buf) {  // bf16 [S1;S2] row f, [Z1;Z2] element f, S0 for the next chunk
-            uint8_t *srow = smem + OFF_SB + buf * TILE;
+        // [S1;S2 | Z] row f (K index f) in the 32-byte-swizzled MN-major tile; S0 / Z0 by chunk mod 3
+        auto publish = [&](int v) {
+            uint8_t *base = smem + OFF_SB + (f >> 3) * SB_SBO + (f & 7) * 32;
+            const uint32_t sw = (uint32_t)((f >> 2) & 1);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4 *>(srow + swz(f, c)) = pack8(S + 8 * c);
-            *reinterpret_cast<__nv_bfloat16 *>(smem + OFF_ZT + buf * ROW1 + row0(f)) = __float2bfloat16_rn(Z);
-            if (f < D) sm.s0f[buf][f] = s0;
-        };
-        if (!SO) publish(0);
-        fence_proxy_async();
-        tc_fence_before();
-        mbar_arrive(&bar[B_SREADY0]);
-        mbar_arrive(&bar[B_DSFREE]);
-        bool ok = true;
-        for (int u = 0; u < U && ok; ++u) {
-            const int bb = u & 1;
-            const int t0 = (c_begin + u) * C;
-            const int n = (u == U - 1) ? n_last : C;
-            // ---- state update
-            if (!mbar_wait(&bar[B_DSFULL], u & 1, ctl, 12)) {
-                ok = false;
-                break;
+            for (int g = 0; g < 4; ++g) {
+                *reinterpret_cast<uint4 *>(base + g * SB_LBO + ((0u ^ sw) << 4)) = pack8(S + 16 * g);
+                *reinterpret_cast<uint4 *>(base + g * SB_LBO + ((1u ^ sw) << 4)) = pack8(S + 16 * g + 8);
             }
-            tc_fence_after();
-            named_bar(2, 128);  // all rows of the previous chunk's output read s0f[bb ^ 1]
-            const float decay = sm.pw[n];
-            {
-                float d[32];
-                tmem_ld32(lane_base + T_DS, d);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) S[e] = fmaf(decay, S[e], d[e]);
-                tmem_ld32(lane_base + T_DS + 32, d);
-                const float2 zs = tmem_ld2(lane_base + T_DZS);
-                tc_fence_before();
-                mbar_arrive(&bar[B_DSFREE]);  // dS is in registers: the next chunk's dS GEMMs may start
-#pragma unroll
-                for (int e = 0; e < 32; ++e) S[32 + e] = fmaf(decay, S[32 + e], d[e]);
-                Z = fmaf(decay, Z, zs.x);
-                if (f < D) s0 = fmaf(decay, s0, zs.y);
-            }
-            const float Z0_in = Z0;
-            Z0 = fmaf(decay, Z0, sm.geo[n]);
-            if (!SO) publish(bb ^ 1);
+            *reinterpret_cast<uint4 *>(base + 4 * SB_LBO + ((0u ^ sw) << 4)) = make_uint4(pack2(Z, 0.f), 0u, 0u, 0u);
+            *reinterpret_cast<uint4 *>(base + 4 * SB_LBO + ((1u ^ sw) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+            if (f < D) sm.s0f[v % 3][f] = s0;
+            if (f == 0) sm.z0f[v % 3] = Z0;
             fence_proxy_async();
-            tc_fence_before();
-            mbar_arrive(&bar[B_SREADY0 + (bb ^ 1)]);
-            if (SO) continue;
-            // ---- output rows
-            if (!mbar_wait(&bar[B_CDONE0 + bb], (u >> 1) & 1, ctl, 14)) {
+            mbar_arrive(&bar[B_SREADY0 + (v & 1)]);
+        };
+        if (!SO && U > 0) publish(0);
+        bool ok = true;
+        for (int u = 0, s = 0; u < U && ok; ++u, s = (s == NST - 1) ? 0 : s + 1) {
+            const int bb = u & 1;
+            const int n = (u == U - 1) ? n_last : C;
+            if (!mbar_wait(&bar[B_PREP0 + s], (u / NST) & 1, ctl, 11) ||
+                !mbar_wait(&bar[B_DSFULL0 + bb], (u >> 1) & 1, ctl, 12)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const int i = f;
-            const float g = sm.pw[i + 1];
-            const float inv = 1.0f / fmaxf(tmem_ld1(lane_base + T_DEN + bb * 16) + g * Z0_in, p.eps);
-            TO *yrow = reinterpret_cast<TO *>(p.y.p) + b * p.y.sb + h * p.y.sh + (int64_t)(t0 + i) * p.y.sl;
-            const float4 *s0in = reinterpret_cast<const float4 *>(sm.s0f[bb]);
+            const float decay = sm.pw[n];
+            const float2 dec2 = make_float2(decay, decay);
+            float ds0 = 0.f;
+            if (f < D) {
 #pragma unroll
-            for (int hcol = 0; hcol < 2; ++hcol) {
-                float acc[32];
-                tmem_ld32(lane_base + T_ACC + bb * 64 + 32 * hcol, acc);
-#pragma unroll
-                for (int e4 = 0; e4 < 8; ++e4) {
-                    const float4 sv = s0in[8 * hcol + e4];
-                    acc[4 * e4 + 0] = fmaf(g, sv.x, acc[4 * e4 + 0]) * inv;
-                    acc[4 * e4 + 1] = fmaf(g, sv.y, acc[4 * e4 + 1]) * inv;
-                    acc[4 * e4 + 2] = fmaf(g, sv.z, acc[4 * e4 + 2]) * inv;
-                    acc[4 * e4 + 3] = fmaf(g, sv.w, acc[4 * e4 + 3]) * inv;
-                }
-                if (i < n) store_row32<TO>(yrow + 32 * hcol, acc);
+                for (int w = 0; w < 4; ++w) ds0 += sm.part[s][w][f];
             }
-            tc_fence_before();
-            mbar_arrive(&bar[B_OEMPTY0 + bb]);
+            const uint32_t dbase = lane_base + T_A + bb * T_AS + 64;  // [dS | dZ] of chunk u
+            const float dz = tmem_ld1(dbase + 64);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+                float d[32];
+                tmem_ld2x16(dbase + 32 * h2, d);
+                if (h2 == 1) {
+                    tc_fence_before();
+                    mbar_arrive(&bar[B_DSFREE0 + bb]);
+                    mbar_arrive(&bar[B_EMPTY0 + s]);
+                }
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const float2 r = __ffma2_rn(dec2, make_float2(S[32 * h2 + e], S[32 * h2 + e + 1]), make_float2(d[e], d[e + 1]));
+                    S[32 * h2 + e] = r.x;
+                    S[32 * h2 + e + 1] = r.y;
+                }
+            }
+            Z = fmaf(decay, Z, dz);
+            if (f < D) s0 = fmaf(decay, s0, ds0);
+            Z0 = fmaf(decay, Z0, sm.geo[n]);
+            if (SO) continue;
+            if (u + 1 < U) {
+                // the carry GEMM of chunk u has finished reading the state tile
+                if (!mbar_wait(&bar[B_QFREE0 + bb], (u >> 1) & 1, ctl, 13)) {
+                    ok = false;
+                    break;
+                }
+                publish(u + 1);
+            }
+            // ---- output rows of chunk u (thread f owns token row f)
+            if (!mbar_wait(&bar[B_CDONE0 + bb], (u >> 1) & 1, ctl, 14) ||
+                !mbar_wait(&bar[B_SREADY0 + bb], (u >> 1) & 1, ctl, 15)) {  // S0 / Z0 entering chunk u
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            {
+                uint32_t r[32], r64;
+                tmem_ld33(lane_base + T_ACC, r, r64);  // columns 0..31 and the denominator column
+                const int s3 = u % 3;
+                const float g = sm.pw[f + 1];
+                const float den = __uint_as_float(r64) + sm.z0f[s3];  // carry + intra-chunk denominator
+                const float sc = g / fmaxf(g * den, p.eps);
+                const float2 sc2 = make_float2(sc, sc);
+                const float4 *s0v = reinterpret_cast<const float4 *>(sm.s0f[s3]);
+                TO *yrow = reinterpret_cast<TO *>(p.y.p) + b * p.y.sb + h * p.y.sh +
+                           (int64_t)((c_begin + u) * C + f) * p.y.sl;
+                auto half = [&](int hc) {  // y in place of the accumulator words
+#pragma unroll
+                    for (int e4 = 0; e4 < 8; ++e4) {
+                        const float4 sv = s0v[8 * hc + e4];
+                        const float2 lo = __fmul2_rn(
+                            __fadd2_rn(make_float2(__uint_as_float(r[4 * e4]), __uint_as_float(r[4 * e4 + 1])),
+                                       make_float2(sv.x, sv.y)),
+                            sc2);
+                        const float2 hi = __fmul2_rn(
+                            __fadd2_rn(make_float2(__uint_as_float(r[4 * e4 + 2]), __uint_as_float(r[4 * e4 + 3])),
+                                       make_float2(sv.z, sv.w)),
+                            sc2);
+                        r[4 * e4] = __float_as_uint(lo.x);
+                        r[4 * e4 + 1] = __float_as_uint(lo.y);
+                        r[4 * e4 + 2] = __float_as_uint(hi.x);
+                        r[4 * e4 + 3] = __float_as_uint(hi.y);
+                    }
+                    if (f < n) store_row32<TO>(yrow + 32 * hc, reinterpret_cast<const float *>(r));
+                };
+                half(0);
+                tmem_ld32_issue(lane_base + T_ACC + 32, r);
+                tmem_wait_ld_regs(r);
+                tc_fence_before();
+                mbar_arrive(&bar[B_OEMPTY]);  // ACC is in registers: the next chunk's carry GEMM may start
+                half(1);
+            }
         }
         // ---- final state
         const bool write_out = ok && !*ctl.abort_flag && p.out.present() &&
