@@ -35,8 +35,14 @@ sys.path.insert(0, HERE)
 PREFILL = dict(B=8, H=12, L=8192, D=64, lam=(0.99, 0.9999), seed=2)
 DECODE = dict(seqs=256, layers=12, H=12, D=64, lam=(0.99, 0.9999), t0=4096, sigma=0.01, seed=3, steps=1000)
 PREFILL_BYTES_PER_TOKHEAD = 8 * 64          # q,k,v in + y out, bf16: 8*D bytes
-PREFILL_FLOP_PER_TOKHEAD = 6 * 64 * 64 + 8 * 64 * 64   # 57,344 (dense-chunk count at C=64)
+# chunked form at C = 128 tokens, F = 2D = 128 moment features, per token-head:
+# scores 2*C*F + intra P.V 2*C*D + carry 2*F*D + state update 2*F*D = 81,920
+PREFILL_FLOP_PER_TOKHEAD = 2 * 128 * 128 + 2 * 128 * 64 + 2 * 128 * 64 + 2 * 128 * 64
 DECODE_BYTES_PER_HEADSTEP = 2 * (2 * 64 * 64 + 3 * 64 + 1) * 4 + 3 * 64 * 2 + 64 * 2  # 67,592
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of
+# each kernel on the bench workload; the commands and the rest of the numbers are in profiles/.
+PREFILL_TRAFFIC = 305_104_896 + 78_318_848    # prefill_tc_kernel<0, bf16>, config 2
+DECODE_TRAFFIC = 1_250_602_000 + 1_183_497_000  # decode_step_kernel<64, bf16, bf16>, config 3
 WORKLOAD = ("config2 prefill: B=8 seqs/GPU, H=12, D=64, L=8192, bf16 q/k/v (QK-normed), fp32 state, "
             "per-head lambda log-U[0.99,0.9999]; step = one pma_prefill (y + final state)")
 
@@ -231,7 +237,7 @@ def bench_prefill(args, ws, rank, device, stream, peaks):
     from prime_moment_attention_b200 import _lib, ops, synth
     hbm_peak, tc_peak, peak_kind = peaks
     c = PREFILL
-    B, H, L, D = c["B"], c["H"], c["L"], c["D"]
+    B, H, L, D = args.prefill_batch or c["B"], c["H"], c["L"], c["D"]
     q, k, v = synth.make_qkv(B, H, L, D, seed=c["seed"] + 1000 * rank, dtype=torch.bfloat16, device=device)
     lam = synth.make_lambdas(H, *c["lam"], seed=c["seed"]).to(device)
     y = torch.empty_like(q)
@@ -242,10 +248,8 @@ def bench_prefill(args, ws, rank, device, stream, peaks):
         ops.prefill(q, k, v, lam, y_out=y, return_state=True)
 
     clocks = ClockSampler(device.index)
-    for _ in range(args.warmup):
-        step()
-    clocks.start()
-    ms = time_steps(step, args.steps, 0, ws, device, stream)
+    clocks.start()  # before the warm-up, so that the timed steps follow it back to back
+    ms = time_steps(step, args.steps, args.warmup, ws, device, stream)
     clk = clocks.stop()
     ms = max_over_ranks(ms, ws, device)
     tokens = B * L * ws
@@ -255,7 +259,9 @@ def bench_prefill(args, ws, rank, device, stream, peaks):
     bw = algo_bytes / (ms * 1e-3) / 1e9
     tf = algo_flop / (ms * 1e-3) / 1e12
     roof = {"bound": "hbm", "achieved": round(bw, 1), "peak": hbm_peak, "unit": "GB/s",
-            "frac": round(bw / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+            "frac": round(bw / hbm_peak, 4),
+            "traffic": PREFILL_TRAFFIC if (B, H, L, D) == (c["B"], c["H"], c["L"], c["D"]) else None,
+            "peak_kind": peak_kind,
             "tensor": {"achieved": round(tf, 1), "peak": tc_peak, "unit": "TFLOP/s", "frac": round(tf / tc_peak, 4)},
             "timed": "whole pma_prefill call (all its launches), CUDA events on the launching stream",
             "algorithmic_bytes_per_launch": algo_bytes, "algorithmic_flop_per_launch": algo_flop}
@@ -309,22 +315,21 @@ def bench_decode(args, ws, rank, device, stream, peaks):
         ops.decode_step(qq, kk, vv, lam_d, st, inplace=True, y_out=yd)
 
     dclk = ClockSampler(device.index)
-    for _ in range(max(3, args.warmup)):
-        dstep()
     dclk.start()
-    dms = max_over_ranks(time_steps(dstep, dc["steps"], 0, ws, device, stream), ws, device)
+    dsteps = args.decode_steps or dc["steps"]
+    dms = max_over_ranks(time_steps(dstep, dsteps, max(3, args.warmup), ws, device, stream), ws, device)
     dclk_r = dclk.stop()
     d_bytes = N * HD * DECODE_BYTES_PER_HEADSTEP
     d_bw = d_bytes / (dms * 1e-3) / 1e9
     return {"metric": "decode_step_us", "value": round(dms * 1e3, 2), "unit": "us/step",
-            "higher_is_better": False, "steps": dc["steps"],
+            "higher_is_better": False, "steps": dsteps,
             "config": {"workload": "config3 decode: 256 seqs x 12 layers x 12 heads per GPU, D=64, bf16 q/k/v, "
                                    "fp32 state in place, all layers' heads in one launch",
                        "state_bytes": N * HD * (2 * 64 * 64 + 3 * 64 + 1) * 4, "l2": "state 1.24 GB > L2"},
             "roofline": {"bound": "hbm", "achieved": round(d_bw, 1), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(d_bw / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "frac": round(d_bw / hbm_peak, 4), "traffic": DECODE_TRAFFIC, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": d_bytes},
-            "gpu_launches": dc["steps"], "clocks": dclk_r}
+            "gpu_launches": dsteps, "clocks": dclk_r}
 
 
 def run_ours(args):
@@ -370,6 +375,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["both", "prefill", "decode"], default="both",
                     help="profiling aid: run only one part (the JSON line then lacks the other)")
+    ap.add_argument("--prefill-batch", type=int, default=0,
+                    help="profiling aid: sequences per GPU for the prefill part (default: config 2's 8)")
+    ap.add_argument("--decode-steps", type=int, default=0,
+                    help="profiling aid: timed decode steps (default 1000)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

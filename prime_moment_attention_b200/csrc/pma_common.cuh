@@ -1,6 +1,8 @@
 // pma_common.cuh -- shared device/host helpers for the PRIME moment attention kernels.
 #pragma once
 
+#include <atomic>
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -8,6 +10,23 @@
 #include "../../include/pma.h"
 
 namespace pma {
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per kernel and device (it is a host
+// round trip; launches repeat it otherwise).  The kernel is a template argument so that every
+// kernel has its own flag word.
+template <auto Kernel>
+inline cudaError_t set_smem_once(int bytes) {
+    static std::atomic<unsigned long long> done{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
+
 
 // ---------------------------------------------------------------------------
 // Element access for the two input/output types (float32, bfloat16).

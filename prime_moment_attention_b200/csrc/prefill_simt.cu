@@ -90,7 +90,7 @@ template <int D, int C, typename TI, typename TO>
 static cudaError_t launch_simt_t(const PrefillParams &p, dim3 grid, cudaStream_t st) {
     const size_t smem = SimtSmem<D, C>::bytes;
     auto kern = prefill_simt_kernel<D, C, TI, TO>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = set_smem_once<prefill_simt_kernel<D, C, TI, TO>>((int)smem);
     if (e != cudaSuccess) return e;
     kern<<<grid, 256, smem, st>>>(p);
     return cudaGetLastError();

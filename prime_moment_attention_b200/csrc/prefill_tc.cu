@@ -975,7 +975,7 @@ template <bool SO, typename TO>
 static cudaError_t launch_t(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
                             const PrefillParams &p, dim3 grid, cudaStream_t st) {
     auto kern = prefill_tc_kernel<SO, TO>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    cudaError_t e = set_smem_once<prefill_tc_kernel<SO, TO>>((int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     kern<<<grid, 512, SMEM_BYTES, st>>>(mq, mk, mv, p);
     return cudaGetLastError();

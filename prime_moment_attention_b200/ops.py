@@ -73,9 +73,18 @@ def _state(st: StateTuple, B: int, H: int, D: int, name: str) -> Tuple[_lib.Stat
 
 
 def new_state(B: int, H: int, D: int, device, zero: bool = True) -> StateTuple:
-    mk = torch.zeros if zero else torch.empty
-    return (mk(B, H, D, device=device), mk(B, H, D, D, device=device), mk(B, H, D, D, device=device),
-            mk(B, H, 1, device=device), mk(B, H, D, device=device), mk(B, H, D, device=device))
+    """(S0, S1, S2, Z0, Z1, Z2) as contiguous slices of one allocation (one allocator call per
+    state; Z0 is placed last so that every other part starts 16-byte aligned)."""
+    BH = B * H
+    flat = (torch.zeros if zero else torch.empty)(BH * (2 * D * D + 3 * D + 1), device=device)
+    o = [0, BH * D, BH * D * (D + 1), BH * D * (2 * D + 1), BH * D * (2 * D + 2), BH * D * (2 * D + 3)]
+    S0 = flat[o[0]:o[1]].view(B, H, D)
+    S1 = flat[o[1]:o[2]].view(B, H, D, D)
+    S2 = flat[o[2]:o[3]].view(B, H, D, D)
+    Z1 = flat[o[3]:o[4]].view(B, H, D)
+    Z2 = flat[o[4]:o[5]].view(B, H, D)
+    Z0 = flat[o[5]:].view(B, H, 1)
+    return (S0, S1, S2, Z0, Z1, Z2)
 
 
 def lambda_tensor(decay: Decay, B: int, H: int, device) -> Tuple[torch.Tensor, int]:
