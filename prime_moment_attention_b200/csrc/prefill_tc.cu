@@ -606,14 +606,20 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll 1
             for (int m = 0; m < nq_pass; ++m) {
                 const int r0 = (q_base + (lane >> 3) + 4 * m) * 4;
+                // row t of the quad is r0 + ((t + lane/8) & 3): the four 8-lane groups of one
+                // access then hit rows with four different swizzle phases (no bank conflicts)
+                const int rg = lane >> 3;
                 float wr[4];
 #pragma unroll
-                for (int t = 0; t < 4; ++t) wr[t] = r0 + t < n ? sm.pw[n - 1 - (r0 + t)] : 0.f;
+                for (int t = 0; t < 4; ++t) {
+                    const int r = r0 + ((t + rg) & 3);
+                    wr[t] = r < n ? sm.pw[n - 1 - r] : 0.f;
+                }
                 uint4 x[4], y[4];
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
-                    x[t] = *reinterpret_cast<const uint4 *>(k_s + swz(r0 + t, cc));
-                    y[t] = *reinterpret_cast<const uint4 *>(v_s + swz(r0 + t, cc));
+                    x[t] = *reinterpret_cast<const uint4 *>(k_s + swz(r0 + ((t + rg) & 3), cc));
+                    y[t] = *reinterpret_cast<const uint4 *>(v_s + swz(r0 + ((t + rg) & 3), cc));
                 }
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
@@ -630,7 +636,7 @@ __global__ void __launch_bounds__(512, 1)
                         o2[c] = as_u(__hmul2(kw, kv));
                         s0p[c] = __ffma2_rn(bf2f(v4[c]), w2, s0p[c]);
                     }
-                    const uint32_t off = swz(r0 + t, cc);
+                    const uint32_t off = swz(r0 + ((t + rg) & 3), cc);
                     *reinterpret_cast<uint4 *>(k_s + off) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
                     *reinterpret_cast<uint4 *>(k2_s + off) = make_uint4(o2[0], o2[1], o2[2], o2[3]);
                 }
