@@ -190,6 +190,25 @@ PMA_API int pma_decode_step(int N, int H, int D,
                     float eps, const pma_seq_tensor *y, pma_stream_t stream);
 
 /*
+ * Decode step over rows of a device-resident state pool: batch row n (q, k, v, y
+ * row n) updates pool row rows[n] in place (pool_in == pool_out) or into pool_out.
+ * The pool holds pool_rows x H head-states in the pma_state layout; rows is a device
+ * int32 array of N entries; entries outside [0, pool_rows) are skipped (y row left
+ * untouched).  Same math and traffic as pma_decode_step.
+ *
+ * Replaces the per-layer state tuples that PrimeMomentCache.get_state/set_state
+ * hand to the decode branch (src/prime_moment_attention/cache.py:15-56,
+ * attention.py:120-143): a serving loop keeps every sequence's state in one pool
+ * and changes the batch by changing `rows`, with no gather/scatter copies.
+ */
+PMA_API int pma_decode_step_rows(int N, int H, int D,
+                                 const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                                 const float *lambda, int64_t lambda_stride_n,
+                                 const int32_t *rows, int pool_rows,
+                                 const pma_state *pool_in, const pma_state *pool_out,
+                                 float eps, const pma_seq_tensor *y, pma_stream_t stream);
+
+/*
  * Segment carry: P <- lambda^len * P + T for B x H head-states, elementwise over
  * all six components.  len = tokens in the segment that produced T.
  * This is the associative step of the reference's inter-chunk scan

@@ -79,6 +79,10 @@ def load() -> ctypes.CDLL:
     L.pma_decode_step.argtypes = ([ctypes.c_int] * 3 + [_P(SeqTensor)] * 3 + [ctypes.c_void_p, ctypes.c_int64]
                                   + [_P(State)] * 2 + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p])
     L.pma_decode_step.restype = ctypes.c_int
+    L.pma_decode_step_rows.argtypes = ([ctypes.c_int] * 3 + [_P(SeqTensor)] * 3 + [ctypes.c_void_p, ctypes.c_int64]
+                                       + [ctypes.c_void_p, ctypes.c_int] + [_P(State)] * 2
+                                       + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p])
+    L.pma_decode_step_rows.restype = ctypes.c_int
     L.pma_state_combine.argtypes = ([ctypes.c_int] * 3 + [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64]
                                     + [_P(State)] * 2 + [ctypes.c_void_p])
     L.pma_state_combine.restype = ctypes.c_int

@@ -16,7 +16,9 @@
 // 32 rows of S1 and S2, keeping 8 rows (16 float4) in flight before it computes.
 // The column partial sums of the two half-warps are joined with one shuffle.
 // Algorithmic traffic per head-state: 2 * (2D^2 + 3D + 1) * 4 bytes of state
-// (read + write) plus q, k, v in and y out.
+// (read + write) plus q, k, v in and y out.  With a row table the state of batch row n
+// is row rows[n] of a larger state pool (serving: sequences keep their pool slot while
+// the batch composition changes); the traffic is the same.
 #include "pma_common.cuh"
 #include "prefill.cuh"
 
@@ -32,9 +34,16 @@ __global__ void __launch_bounds__(256) decode_step_kernel(const DecodeParams p) 
 
     __shared__ float sq[8][D], sk[8][D];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int idx = blockIdx.x * 8 + warp;          // head-state index n*H + h
-    if (idx >= p.N * p.H) return;
-    const int n = idx / p.H, h = idx - n * p.H;
+    const int bidx = blockIdx.x * 8 + warp;         // batch row n and head h: n*H + h
+    if (bidx >= p.N * p.H) return;
+    const int n = bidx / p.H, h = bidx - n * p.H;
+    // state row: n itself, or rows[n] of a state pool (rows outside the pool are skipped)
+    int srow = n;
+    if (p.rows) {
+        srow = p.rows[n];
+        if (srow < 0 || srow >= p.pool_rows) return;
+    }
+    const int idx = srow * p.H + h;                  // head-state index in the state arrays
     const float lam = p.lambda[(int64_t)n * p.lam_sn + h];
 
     const TI *qp = reinterpret_cast<const TI *>(p.q.p) + n * p.q.sb + h * p.q.sh;

@@ -293,6 +293,42 @@ int pma_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_
     return e == cudaSuccess ? PMA_OK : cuda_fail(e);
 }
 
+int pma_decode_step_rows(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                         const pma_seq_tensor *v, const float *lambda, int64_t lambda_stride_n, const int32_t *rows,
+                         int pool_rows, const pma_state *pool_in, const pma_state *pool_out, float eps,
+                         const pma_seq_tensor *y, pma_stream_t stream) {
+    if (N < 0 || H <= 0 || !lambda || lambda_stride_n < 0 || pool_rows < 0) return PMA_ERR_ARGUMENT;
+    if (N > 0 && !rows) return PMA_ERR_ARGUMENT;
+    if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
+    int rc;
+    const bool empty = N == 0;
+    if ((rc = check_seq(q, false, empty)) || (rc = check_seq(k, false, empty)) || (rc = check_seq(v, false, empty)) ||
+        (rc = check_seq(y, false, empty)))
+        return rc;
+    if (q->dtype != k->dtype || q->dtype != v->dtype) return PMA_ERR_DTYPE;
+    if ((rc = check_state(pool_in)) || (rc = check_state(pool_out))) return rc;
+    DevInfo di;
+    if ((rc = device_info(&di))) return rc;
+    if (N == 0) return PMA_OK;
+    if ((long)N * H > (1L << 30) || (long)pool_rows * H > (1L << 30)) return PMA_ERR_ARGUMENT;
+    DecodeParams p{};
+    p.N = N;
+    p.H = H;
+    p.q = seq_of(q);
+    p.k = seq_of(k);
+    p.v = seq_of(v);
+    p.y = seqout_of(y);
+    p.lambda = lambda;
+    p.lam_sn = lambda_stride_n;
+    p.in = *pool_in;
+    p.out = *pool_out;
+    p.eps = eps;
+    p.rows = rows;
+    p.pool_rows = pool_rows;
+    cudaError_t e = launch_decode(p, D, q->dtype, y->dtype, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? PMA_OK : cuda_fail(e);
+}
+
 int pma_state_combine(int B, int H, int D, const float *lambda, int64_t lambda_stride_b, int64_t len,
                       const pma_state *T, const pma_state *P, pma_stream_t stream) {
     if (B < 0 || H <= 0 || !lambda || lambda_stride_b < 0 || len < 0) return PMA_ERR_ARGUMENT;

@@ -33,6 +33,8 @@ struct DecodeParams {
     int64_t lam_sn;
     pma_state in, out;
     float eps;
+    const int32_t *rows;    // nullable: state row of batch row n (a state pool), else n
+    int pool_rows;          // rows in the pool (bounds for `rows`)
 };
 
 cudaError_t launch_decode(const DecodeParams &p, int D, int idt, int ydt, cudaStream_t s);

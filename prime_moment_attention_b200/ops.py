@@ -202,6 +202,41 @@ def decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
     return y, st_out_t
 
 
+def decode_step_rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay, pool: StateTuple,
+                     rows: torch.Tensor, eps: float = 1.0, out_dtype: Optional[torch.dtype] = None,
+                     y_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One recurrent step for batch rows n = 0..N-1 whose states are rows rows[n] of `pool`.
+
+    `pool` is a state tuple [P, H, ...] (contiguous float32, updated in place); `rows` an int32
+    CUDA tensor [N] of pool rows (rows outside [0, P) are skipped and their y rows untouched).
+    Returns y [N, H, D]."""
+    dev = _require_cuda(q, k, v)
+    if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must share one [N,H,D] shape")
+    N, H, D = q.shape
+    P = pool[0].shape[0]
+    if rows.dtype != torch.int32 or rows.dim() != 1 or rows.shape[0] != N or rows.device != dev:
+        raise ValueError("rows must be an int32 tensor [N] on the inputs' device")
+    rows = rows.contiguous()
+    L_ = _lib.load()
+    qs, q = _seq(q, False)
+    ks, k = _seq(k, False)
+    vs, v = _seq(v, False)
+    lam, lam_sn = lambda_tensor(decay, N, H, dev)
+    pool_c, pool_t = _state(pool, P, H, D, "pool")
+    if not all(a.data_ptr() == b.data_ptr() for a, b in zip(pool_t, pool)):
+        raise ValueError("the pool must be contiguous float32 (it is updated in place)")
+    y = y_out if y_out is not None else torch.empty(N, H, D, dtype=out_dtype or q.dtype, device=dev)
+    ys, y2 = _seq(y, False)
+    if y2 is not y:
+        raise ValueError("y_out must have a contiguous, 16-byte aligned last axis")
+    rc = L_.pma_decode_step_rows(N, H, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(), lam_sn,
+                                 rows.data_ptr(), P, ctypes.byref(pool_c), ctypes.byref(pool_c), float(eps),
+                                 ctypes.byref(ys), _stream(dev))
+    _lib.check("pma_decode_step_rows", rc)
+    return y
+
+
 def state_combine(T: StateTuple, P: StateTuple, decay: Decay, length: int) -> StateTuple:
     """P <- decay^length * P + T in place (P must be contiguous float32); returns P."""
     dev = _require_cuda(T[1], P[1])

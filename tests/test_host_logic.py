@@ -96,3 +96,26 @@ def test_cache_api_matches_reference():
     assert cache.get_seq_length() == 5
     cache.reset()
     assert cache.get_state(0) is None and cache.get_seq_length() == 0
+
+
+def test_state_pool_slot_bookkeeping_without_gpu(monkeypatch):
+    """Slot allocation, release and row numbering of StatePool (device tensors replaced by CPU)."""
+    import torch
+    from prime_moment_attention_b200 import ops, pool as P
+    real_new = ops.new_state
+    monkeypatch.setattr(ops, "new_state", lambda B, H, D, device, zero=True: real_new(B, H, D, "cpu", zero))
+    pool = P.StatePool(capacity=4, H=2, D=8, layers=3, device="cpu")
+    a, b = pool.alloc(), pool.alloc()
+    assert (a, b) == (0, 1) and pool.free_slots == 2
+    pool.get_state(2, b)[1].fill_(1.0)
+    assert float(pool.state[1][2 * 4 + b].sum()) == 2 * 8 * 8
+    assert pool.rows(2, [b, a]).tolist() == [9, 8]
+    pool.release(a)
+    import pytest
+    with pytest.raises(ValueError):
+        pool.release(a)
+    c = pool.alloc()
+    assert c == a
+    pool.release(b)
+    d = pool.alloc()  # reuse zeroes the slot's rows in every layer
+    assert d == b and float(pool.state[1][2 * 4 + b].sum()) == 0.0
