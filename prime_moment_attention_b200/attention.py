@@ -132,4 +132,13 @@ class PrimeMomentAttention(nn.Module):
             self.q_norm = nn.LayerNorm(head_dim)
             self.k_norm = nn.LayerNorm(head_dim)
 
+    def _apply(self, fn, recurse=True):
+        # Module.to(bfloat16) / .half() would round the per-head decays (0.9995 -> 1.0 in
+        # bf16); they stay float32 and only follow the device, like the reference's float decay.
+        lam = self.decay_per_head
+        super()._apply(fn, recurse)
+        if lam is not None and self.decay_per_head.dtype != torch.float32:
+            self.decay_per_head = lam.to(self.decay_per_head.device, torch.float32)
+        return self
+
     forward = moment_forward

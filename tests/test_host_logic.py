@@ -119,3 +119,14 @@ def test_state_pool_slot_bookkeeping_without_gpu(monkeypatch):
     pool.release(b)
     d = pool.alloc()  # reuse zeroes the slot's rows in every layer
     assert d == b and float(pool.state[1][2 * 4 + b].sum()) == 0.0
+
+
+def test_module_dtype_cast_keeps_per_head_decay_float32():
+    """.to(bfloat16) / .half() cast the projections but not the per-head decays."""
+    import torch
+    from prime_moment_attention_b200 import attention as A
+    m = A.PrimeMomentAttention(64, 2, 32, decay=[0.9995, 0.999]).to(torch.bfloat16)
+    assert m.q_proj.weight.dtype == torch.bfloat16
+    assert m.decay_per_head.dtype == torch.float32
+    assert m.decay_per_head.tolist() == torch.tensor([0.9995, 0.999]).tolist()
+    assert m.half().decay_per_head.dtype == torch.float32
