@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define PMA_ABI_VERSION 1
+#define PMA_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define PMA_API __attribute__((visibility("default")))
@@ -87,6 +87,32 @@ typedef struct {
     float *Z1;   /* [B, H, D]                       */
     float *Z2;   /* [B, H, D]                       */
 } pma_state;
+
+/*
+ * Optional per-call input prologue: the module work between the q/k/v projections
+ * and the core (attention.py:87-101), folded into the kernels' load stage so the
+ * projection outputs are read once, in place:
+ *   - GQA: k and v hold H / kv_groups heads; query head h reads kv head
+ *     h / kv_groups, which is what k.repeat_interleave(kv_groups, dim=1) gives
+ *     (attention.py:92-94), without the copy;
+ *   - LayerNorm over the head dim with affine weight/bias on q and on k
+ *     (nn.LayerNorm(head_dim), attention.py:73-75, 96-98): biased variance,
+ *     y = (x - mean) / sqrt(var + norm_eps) * weight + bias;
+ *   - q scaled by q_scale after its norm (1/sqrt(D), attention.py:101).
+ * The prologue is computed in float32 from the input elements; with bf16 inputs
+ * the normalised, scaled q and k are rounded to bf16 once before the tensor-core
+ * products (the reference rounds after the norm and again after the scale).
+ * Weights and biases are device float32 arrays of D elements.
+ */
+typedef struct {
+    int32_t kv_groups;            /* >= 1 */
+    float q_scale;                /* 1.0f: q used as given */
+    const float *q_norm_weight;   /* NULL: no LayerNorm on q */
+    const float *q_norm_bias;     /* NULL: zero bias */
+    const float *k_norm_weight;   /* NULL: no LayerNorm on k */
+    const float *k_norm_bias;     /* NULL: zero bias */
+    float norm_eps;               /* LayerNorm eps (nn.LayerNorm default 1e-5) */
+} pma_prologue;
 
 /* ABI version (PMA_ABI_VERSION of the built library). */
 PMA_API int pma_version(void);
@@ -207,6 +233,50 @@ PMA_API int pma_decode_step_rows(int N, int H, int D,
                                  const int32_t *rows, int pool_rows,
                                  const pma_state *pool_in, const pma_state *pool_out,
                                  float eps, const pma_seq_tensor *y, pma_stream_t stream);
+
+/*
+ * Bytes of scratch pma_prefill_ex needs (0 if none): pma_prefill_workspace_bytes
+ * plus, on the tensor-core path (bf16, D = 64) with a LayerNorm in the prologue, room
+ * for the normalised bf16 q and/or k rows (2 * D bytes per row).
+ */
+PMA_API size_t pma_prefill_ex_workspace_bytes(int B, int H, int L, int D, int dtype,
+                                              const pma_prologue *prologue);
+
+/*
+ * pma_prefill with an input prologue (GQA head map, LayerNorm QK-norm, q scale):
+ * the module forward of attention.py:86-207 minus the projection GEMMs.  q is the
+ * raw q projection [B,H,L,D]; k and v are the raw k/v projections with
+ * H / prologue->kv_groups heads (typically transposed views of [B,L,Hkv,D]).
+ * prologue NULL is the identity prologue (= pma_prefill).  workspace: at least
+ * pma_prefill_ex_workspace_bytes(...).  Other arguments and results as pma_prefill;
+ * PMA_ERR_ARGUMENT if kv_groups < 1 or does not divide H.
+ * The CUDA-core kernels apply the prologue as they load rows.  The tensor-core kernel
+ * applies the GQA map in its tensor-map coordinates and a bf16-exact q_scale in its prep
+ * warps; LayerNorms (and a q_scale bf16 cannot hold) run first as one HBM pass that writes
+ * the normalised rows into the workspace (128 bytes read + 128 written per row).
+ */
+PMA_API int pma_prefill_ex(int B, int H, int L, int D,
+                           const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                           const pma_prologue *prologue,
+                           const float *lambda, int64_t lambda_stride_b,
+                           const pma_state *state_in, const pma_state *state_out,
+                           float eps, const pma_seq_tensor *y,
+                           void *workspace, size_t workspace_bytes, pma_stream_t stream);
+
+/*
+ * Decode step with an input prologue and an optional state-pool row table: the
+ * L == 1 module branch (attention.py:86-143, 205) minus the projection GEMMs.
+ * k and v have H / prologue->kv_groups heads.  rows NULL: batch row n uses state
+ * row n (as pma_decode_step, state arrays of N x H head-states); else as
+ * pma_decode_step_rows with pool_rows rows.  prologue NULL is the identity.
+ */
+PMA_API int pma_decode_step_ex(int N, int H, int D,
+                               const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                               const pma_prologue *prologue,
+                               const float *lambda, int64_t lambda_stride_n,
+                               const int32_t *rows, int pool_rows,
+                               const pma_state *state_in, const pma_state *state_out,
+                               float eps, const pma_seq_tensor *y, pma_stream_t stream);
 
 /*
  * Segment carry: P <- lambda^len * P + T for B x H head-states, elementwise over

@@ -37,6 +37,14 @@ class State(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in ("S0", "S1", "S2", "Z0", "Z1", "Z2")]
 
 
+class Prologue(ctypes.Structure):
+    """pma_prologue: GQA head map, LayerNorm QK-norm and q scale folded into the kernels."""
+    _fields_ = [("kv_groups", ctypes.c_int32), ("q_scale", ctypes.c_float),
+                ("q_norm_weight", ctypes.c_void_p), ("q_norm_bias", ctypes.c_void_p),
+                ("k_norm_weight", ctypes.c_void_p), ("k_norm_bias", ctypes.c_void_p),
+                ("norm_eps", ctypes.c_float)]
+
+
 _P = ctypes.POINTER
 _lib = None
 
@@ -83,6 +91,16 @@ def load() -> ctypes.CDLL:
                                        + [ctypes.c_void_p, ctypes.c_int] + [_P(State)] * 2
                                        + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p])
     L.pma_decode_step_rows.restype = ctypes.c_int
+    L.pma_prefill_ex_workspace_bytes.argtypes = [ctypes.c_int] * 5 + [_P(Prologue)]
+    L.pma_prefill_ex_workspace_bytes.restype = ctypes.c_size_t
+    L.pma_prefill_ex.argtypes = ([ctypes.c_int] * 4 + [_P(SeqTensor)] * 3 + [_P(Prologue)]
+                                 + [ctypes.c_void_p, ctypes.c_int64] + [_P(State)] * 2
+                                 + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p])
+    L.pma_prefill_ex.restype = ctypes.c_int
+    L.pma_decode_step_ex.argtypes = ([ctypes.c_int] * 3 + [_P(SeqTensor)] * 3 + [_P(Prologue)]
+                                     + [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int]
+                                     + [_P(State)] * 2 + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p])
+    L.pma_decode_step_ex.restype = ctypes.c_int
     L.pma_state_combine.argtypes = ([ctypes.c_int] * 3 + [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64]
                                     + [_P(State)] * 2 + [ctypes.c_void_p])
     L.pma_state_combine.restype = ctypes.c_int

@@ -4,8 +4,12 @@ Mirrors, with the same names, arguments and return values:
   * PrimeMomentAttention          src/prime_moment_attention/attention.py:42-210
   * chunked_prime_ssd_core        src/prime_moment_attention/chunked_ssd.py:48-184
 
-The projections, GQA repeat, LayerNorm QK-norm and 1/sqrt(D) scale stay in PyTorch
-(cuBLAS) exactly as the reference writes them (attention.py:86-101).  The three
+The projections stay in PyTorch (cuBLAS).  The GQA repeat, LayerNorm QK-norm and
+1/sqrt(D) scale of attention.py:92-101 are folded into the kernels' load stage
+(ops.Prologue / pma_prologue): the kernels read the projection outputs in place and
+no repeated, normalised or scaled copy of q, k, v is written.  (When the norms are
+not nn.LayerNorm over head_dim with one shared eps, PyTorch applies them as the
+reference writes them and only the core runs on the kernels.)  The three
 L branches of the reference (decode L == 1, dense 1 < L <= chunk_threshold,
 chunked L > chunk_threshold) all go to the CUDA kernels: decode to
 pma_decode_step, both prefill branches to pma_prefill, whose result does not
@@ -48,6 +52,35 @@ def chunked_prime_ssd_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return y, st
 
 
+def _prologue(self) -> Optional[ops.Prologue]:
+    """The module's GQA map, QK-norm and scale as a kernel prologue; None when use_qk_norm is
+    set with norms other than nn.LayerNorm(head_dim) sharing one eps.  float32 copies of
+    bf16 norm parameters are cached on the module, keyed on the parameters' storage and
+    version counter (an in-place weight update invalidates them)."""
+    D = self.head_dim
+    kw = dict(kv_groups=self.num_kv_groups, q_scale=self.scaling)
+    if not self.use_qk_norm:
+        return ops.Prologue(**kw)
+    qn, kn = self.q_norm, self.k_norm
+    if not (isinstance(qn, nn.LayerNorm) and isinstance(kn, nn.LayerNorm) and tuple(qn.normalized_shape) == (D,)
+            and tuple(kn.normalized_shape) == (D,) and qn.eps == kn.eps):
+        return None
+    params = (qn.weight, qn.bias, kn.weight, kn.bias)
+    key = tuple(None if t is None else (t.data_ptr(), t._version, t.dtype, t.device) for t in params)
+    cached = getattr(self, "_pma_norm_cache", None)
+    if cached is None or cached[0] != key:
+        dev = self.q_proj.weight.device
+        ones = torch.ones(D, dtype=torch.float32, device=dev)
+        f32 = [None if t is None else t.detach().to(torch.float32).contiguous() for t in params]
+        f32[0] = ones if f32[0] is None else f32[0]  # elementwise_affine=False: unit weight
+        f32[2] = ones if f32[2] is None else f32[2]
+        cached = (key, f32)
+        self._pma_norm_cache = cached
+    w = cached[1]
+    return ops.Prologue(q_norm_weight=w[0], q_norm_bias=w[1], k_norm_weight=w[2], k_norm_bias=w[3],
+                        norm_eps=qn.eps, **kw)
+
+
 def moment_forward(self, hidden_states: torch.Tensor, state: Optional[Tuple[torch.Tensor, ...]] = None,
                    return_state: bool = False):
     """PrimeMomentAttention.forward on the CUDA kernels.
@@ -65,13 +98,14 @@ def moment_forward(self, hidden_states: torch.Tensor, state: Optional[Tuple[torc
     q = self.q_proj(hidden_states).view(B, L, H, D).transpose(1, 2)
     k = self.k_proj(hidden_states).view(B, L, self.num_kv_heads, D).transpose(1, 2)
     v = self.v_proj(hidden_states).view(B, L, self.num_kv_heads, D).transpose(1, 2)
-    if self.num_kv_groups > 1:
-        k = k.repeat_interleave(self.num_kv_groups, dim=1)
-        v = v.repeat_interleave(self.num_kv_groups, dim=1)
-    if self.use_qk_norm:
+    pro = _prologue(self)
+    if pro is None:  # norms the kernels do not fold: the reference's own sequence
+        if self.num_kv_groups > 1:
+            k = k.repeat_interleave(self.num_kv_groups, dim=1)
+            v = v.repeat_interleave(self.num_kv_groups, dim=1)
         q = self.q_norm(q)
         k = self.k_norm(k)
-    q = q * self.scaling
+        q = q * self.scaling
     if q.dtype not in (torch.float32, torch.bfloat16):
         q, k, v = q.float(), k.float(), v.float()
 
@@ -83,14 +117,14 @@ def moment_forward(self, hidden_states: torch.Tensor, state: Optional[Tuple[torc
             state = ops.new_state(B, H, D, hidden_states.device)
         y, next_state = ops.decode_step(q[:, :, 0], k[:, :, 0], v[:, :, 0], decay, state, eps=self.eps,
                                         out_dtype=orig_dtype if orig_dtype in (torch.float32, torch.bfloat16)
-                                        else torch.float32)
+                                        else torch.float32, prologue=pro)
         y = y.to(orig_dtype).reshape(B, 1, H * D)
     else:
         out_dt = orig_dtype if orig_dtype in (torch.float32, torch.bfloat16) else torch.float32
         # write y straight into [B, L, H, D] so the o_proj input needs no transpose copy
         y_bl = torch.empty(B, L, H, D, dtype=out_dt, device=hidden_states.device)
         _, next_state = ops.prefill(q, k, v, decay, state=state, eps=self.eps, return_state=return_state,
-                                    y_out=y_bl.transpose(1, 2))
+                                    y_out=y_bl.transpose(1, 2), prologue=pro)
         y = y_bl.to(orig_dtype).view(B, L, H * D)
     output = self.o_proj(y)
     return output, (next_state if return_state else None)

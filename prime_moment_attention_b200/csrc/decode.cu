@@ -47,11 +47,23 @@ __global__ void __launch_bounds__(256) decode_step_kernel(const DecodeParams p) 
     const float lam = p.lambda[(int64_t)n * p.lam_sn + h];
 
     const TI *qp = reinterpret_cast<const TI *>(p.q.p) + n * p.q.sb + h * p.q.sh;
-    const TI *kp = reinterpret_cast<const TI *>(p.k.p) + n * p.k.sb + h * p.k.sh;
-    const TI *vp = reinterpret_cast<const TI *>(p.v.p) + n * p.v.sb + h * p.v.sh;
+    const int hk = h / p.pro.groups;                 // GQA: the kv head this query head reads
+    const TI *kp = reinterpret_cast<const TI *>(p.k.p) + n * p.k.sb + hk * p.k.sh;
+    const TI *vp = reinterpret_cast<const TI *>(p.v.p) + n * p.v.sb + hk * p.v.sh;
     for (int d = lane; d < D; d += 32) {
         sq[warp][d] = Elem<TI>::to_f(qp[d]);
         sk[warp][d] = Elem<TI>::to_f(kp[d]);
+    }
+    __syncwarp();
+    // prologue: q -> LN(q) * scale, k -> LN(k); each lane rewrites the elements it loaded
+    if (p.pro.q_work()) {
+        const float2 st = p.pro.qw ? warp_row_stats<D>(sq[warp], p.pro.ln_eps, lane) : make_float2(0.f, 1.f);
+        for (int d = lane; d < D; d += 32)
+            sq[warp][d] = prologue_elem(sq[warp][d], st, p.pro.qw, p.pro.qb, d, p.pro.q_scale);
+    }
+    if (p.pro.k_work()) {
+        const float2 st = warp_row_stats<D>(sk[warp], p.pro.ln_eps, lane);
+        for (int d = lane; d < D; d += 32) sk[warp][d] = prologue_elem(sk[warp][d], st, p.pro.kw, p.pro.kb, d, 1.f);
     }
     __syncwarp();
 

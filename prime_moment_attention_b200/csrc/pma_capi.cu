@@ -1,5 +1,6 @@
 // pma_capi.cu -- the extern "C" entry points declared in include/pma.h:
 // argument validation on the host, planning (kernel, chunk, segments) and launch.
+#include <cstring>
 #include <mutex>
 
 #include "prefill.cuh"
@@ -121,6 +122,68 @@ Plan make_plan(int B, int H, int L, int D, int dtype, int sms) {
     return p;
 }
 
+// pma_prologue -> kernel view; NULL is the identity (no GQA, no norm, scale 1).
+int prologue_of(const pma_prologue *pp, int H, Prologue *out) {
+    Prologue r{1, 1.0f, nullptr, nullptr, nullptr, nullptr, 1e-5f};
+    if (pp) {
+        if (pp->kv_groups < 1 || H % pp->kv_groups) return PMA_ERR_ARGUMENT;
+        if (!(pp->norm_eps >= 0.0f) || pp->q_scale != pp->q_scale) return PMA_ERR_ARGUMENT;
+        const float *ptrs[4] = {pp->q_norm_weight, pp->q_norm_bias, pp->k_norm_weight, pp->k_norm_bias};
+        for (const float *f : ptrs)
+            if (reinterpret_cast<uintptr_t>(f) % 4) return PMA_ERR_LAYOUT;
+        r.groups = pp->kv_groups;
+        r.q_scale = pp->q_scale;
+        r.qw = pp->q_norm_weight;
+        r.qb = pp->q_norm_weight ? pp->q_norm_bias : nullptr;
+        r.kw = pp->k_norm_weight;
+        r.kb = pp->k_norm_weight ? pp->k_norm_bias : nullptr;
+        r.ln_eps = pp->norm_eps;
+    }
+    *out = r;
+    return PMA_OK;
+}
+
+int prefill_impl(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                 const pma_seq_tensor *v, const pma_prologue *prologue, const float *lambda,
+                 int64_t lambda_stride_b, const pma_state *state_in, const pma_state *state_out, float eps,
+                 const pma_seq_tensor *y, void *workspace, size_t workspace_bytes, pma_stream_t stream);
+int decode_impl(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                const pma_prologue *prologue, const float *lambda, int64_t lambda_stride_n, const int32_t *rows,
+                int pool_rows, const pma_state *state_in, const pma_state *state_out, float eps,
+                const pma_seq_tensor *y, pma_stream_t stream);
+
+bool bf16_exact(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return (u & 0xffffu) == 0;
+}
+
+// Tensor-core path: which inputs the QK-norm pass rewrites, and the workspace beyond the plan's.
+struct ProPass {
+    bool q = false, k = false;
+    size_t q_off = 0, k_off = 0, total = 0;  // byte offsets of the copies in the workspace; total bytes
+};
+
+ProPass pro_pass(const Plan &pl, const Prologue &pro, int B, int H, int L, bool want_y) {
+    ProPass r;
+    r.total = pl.ws_bytes;
+    if (!pl.tc) return r;  // the CUDA-core kernel folds the prologue into its loads
+    r.q = want_y && (pro.qw != nullptr || (pro.q_scale != 1.0f && !bf16_exact(pro.q_scale)));
+    r.k = pro.kw != nullptr;
+    size_t off = (pl.ws_bytes + 255) / 256 * 256;
+    if (r.q) {
+        r.q_off = off;
+        off += (size_t)B * H * L * 64 * 2;
+    }
+    if (r.k) {
+        off = (off + 255) / 256 * 256;
+        r.k_off = off;
+        off += (size_t)B * (H / pro.groups) * L * 64 * 2;
+    }
+    if (r.q || r.k) r.total = off;
+    return r;
+}
+
 cudaError_t launch_prefill(const Plan &pl, const PrefillParams &p, int D, int idt, int ydt, dim3 grid,
                            cudaStream_t st) {
     return pl.tc ? launch_prefill_tc(p, ydt, grid, st) : launch_prefill_simt(p, D, idt, ydt, grid, st);
@@ -167,13 +230,68 @@ size_t pma_prefill_workspace_bytes(int B, int H, int L, int D, int dtype) {
     return make_plan(B, H, L, D, dtype, di.sms).ws_bytes;
 }
 
+size_t pma_prefill_ex_workspace_bytes(int B, int H, int L, int D, int dtype, const pma_prologue *prologue) {
+    if (B <= 0 || H <= 0 || L <= 0 || !supported_d(D) || !supported_dtype(dtype)) return 0;
+    Prologue pro;
+    if (prologue_of(prologue, H, &pro) != PMA_OK) return 0;
+    DevInfo di;
+    if (device_info(&di) != PMA_OK) return 0;
+    return pro_pass(make_plan(B, H, L, D, dtype, di.sms), pro, B, H, L, true).total;
+}
+
 int pma_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
                 const pma_seq_tensor *v, const float *lambda, int64_t lambda_stride_b, const pma_state *state_in,
                 const pma_state *state_out, float eps, const pma_seq_tensor *y, void *workspace,
                 size_t workspace_bytes, pma_stream_t stream) {
+    return prefill_impl(B, H, L, D, q, k, v, nullptr, lambda, lambda_stride_b, state_in, state_out, eps, y,
+                        workspace, workspace_bytes, stream);
+}
+
+int pma_prefill_ex(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                   const pma_seq_tensor *v, const pma_prologue *prologue, const float *lambda,
+                   int64_t lambda_stride_b, const pma_state *state_in, const pma_state *state_out, float eps,
+                   const pma_seq_tensor *y, void *workspace, size_t workspace_bytes, pma_stream_t stream) {
+    return prefill_impl(B, H, L, D, q, k, v, prologue, lambda, lambda_stride_b, state_in, state_out, eps, y,
+                        workspace, workspace_bytes, stream);
+}
+
+int pma_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                    const float *lambda, int64_t lambda_stride_n, const pma_state *state_in,
+                    const pma_state *state_out, float eps, const pma_seq_tensor *y, pma_stream_t stream) {
+    return decode_impl(N, H, D, q, k, v, nullptr, lambda, lambda_stride_n, nullptr, 0, state_in, state_out, eps, y,
+                       stream);
+}
+
+int pma_decode_step_rows(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                         const pma_seq_tensor *v, const float *lambda, int64_t lambda_stride_n, const int32_t *rows,
+                         int pool_rows, const pma_state *pool_in, const pma_state *pool_out, float eps,
+                         const pma_seq_tensor *y, pma_stream_t stream) {
+    if (N > 0 && !rows) return PMA_ERR_ARGUMENT;
+    return decode_impl(N, H, D, q, k, v, nullptr, lambda, lambda_stride_n, rows, pool_rows, pool_in, pool_out, eps,
+                       y, stream);
+}
+
+int pma_decode_step_ex(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                       const pma_seq_tensor *v, const pma_prologue *prologue, const float *lambda,
+                       int64_t lambda_stride_n, const int32_t *rows, int pool_rows, const pma_state *state_in,
+                       const pma_state *state_out, float eps, const pma_seq_tensor *y, pma_stream_t stream) {
+    return decode_impl(N, H, D, q, k, v, prologue, lambda, lambda_stride_n, rows, pool_rows, state_in, state_out,
+                       eps, y, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+int prefill_impl(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                 const pma_seq_tensor *v, const pma_prologue *prologue, const float *lambda,
+                 int64_t lambda_stride_b, const pma_state *state_in, const pma_state *state_out, float eps,
+                 const pma_seq_tensor *y, void *workspace, size_t workspace_bytes, pma_stream_t stream) {
     if (B < 0 || H <= 0 || L < 0 || !lambda || lambda_stride_b < 0) return PMA_ERR_ARGUMENT;
     if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
     int rc;
+    Prologue pro;
+    if ((rc = prologue_of(prologue, H, &pro))) return rc;
     const bool empty = (L == 0 || B == 0);  // no element is touched: null data is fine
     if ((rc = check_seq(q, true, empty)) || (rc = check_seq(k, true, empty)) || (rc = check_seq(v, true, empty)))
         return rc;
@@ -206,8 +324,9 @@ int pma_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_s
     }
 
     const Plan pl = make_plan(B, H, L, D, q->dtype, di.sms);
-    if (pl.ws_bytes && (!workspace || workspace_bytes < pl.ws_bytes)) return PMA_ERR_WORKSPACE;
-    if (pl.ws_bytes && reinterpret_cast<uintptr_t>(workspace) % 16) return PMA_ERR_WORKSPACE;
+    const ProPass pp = pro_pass(pl, pro, B, H, L, y != nullptr);
+    if (pp.total && (!workspace || workspace_bytes < pp.total)) return PMA_ERR_WORKSPACE;
+    if (pp.total && reinterpret_cast<uintptr_t>(workspace) % 16) return PMA_ERR_WORKSPACE;
     if (!y && !state_out) return PMA_OK;  // nothing requested
     const int ydt = y ? y->dtype : PMA_F32;
 
@@ -219,13 +338,31 @@ int pma_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_s
     p.q = seq_of(q);
     p.k = seq_of(k);
     p.v = seq_of(v);
+    p.pro = pro;
+    cudaError_t e;
+    if (pl.tc) {  // norms (and a scale bf16 cannot hold) by the QK-norm pass; the core keeps the GQA map
+        char *wsb = reinterpret_cast<char *>(workspace);
+        const int hkv = H / pro.groups;
+        if (pp.q) {
+            e = launch_qk_norm(p.q, B, H, L, pro.qw, pro.qb, pro.ln_eps, pro.q_scale, wsb + pp.q_off, di.sms, st);
+            if (e != cudaSuccess) return cuda_fail(e);
+            p.q = Seq{wsb + pp.q_off, (int64_t)H * L * 64, (int64_t)L * 64, 64};
+            p.pro.q_scale = 1.0f;
+        }
+        if (pp.k) {
+            e = launch_qk_norm(p.k, B, hkv, L, pro.kw, pro.kb, pro.ln_eps, 1.0f, wsb + pp.k_off, di.sms, st);
+            if (e != cudaSuccess) return cuda_fail(e);
+            p.k = Seq{wsb + pp.k_off, (int64_t)hkv * L * 64, (int64_t)L * 64, 64};
+        }
+        p.pro.qw = p.pro.qb = p.pro.kw = p.pro.kb = nullptr;
+        if (!y) p.pro.q_scale = 1.0f;
+    }
     p.y = seqout_of(y);
     p.lambda = lambda;
     p.lam_sb = lambda_stride_b;
     p.eps = eps;
     p.status = nullptr;
 
-    cudaError_t e;
     if (pl.ws_bytes) {  // clear the status word the tensor-core kernel reports timeouts in
         p.status = reinterpret_cast<int *>(workspace);
         if ((e = cudaMemsetAsync(p.status, 0, sizeof(int), st)) != cudaSuccess) return cuda_fail(e);
@@ -261,52 +398,21 @@ int pma_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_s
     return e == cudaSuccess ? PMA_OK : cuda_fail(e);
 }
 
-int pma_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
-                    const float *lambda, int64_t lambda_stride_n, const pma_state *state_in,
-                    const pma_state *state_out, float eps, const pma_seq_tensor *y, pma_stream_t stream) {
-    if (N < 0 || H <= 0 || !lambda || lambda_stride_n < 0) return PMA_ERR_ARGUMENT;
+int decode_impl(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                const pma_prologue *prologue, const float *lambda, int64_t lambda_stride_n, const int32_t *rows,
+                int pool_rows, const pma_state *state_in, const pma_state *state_out, float eps,
+                const pma_seq_tensor *y, pma_stream_t stream) {
+    if (N < 0 || H <= 0 || !lambda || lambda_stride_n < 0 || pool_rows < 0) return PMA_ERR_ARGUMENT;
     if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
     int rc;
+    Prologue pro;
+    if ((rc = prologue_of(prologue, H, &pro))) return rc;
     const bool empty = N == 0;
     if ((rc = check_seq(q, false, empty)) || (rc = check_seq(k, false, empty)) || (rc = check_seq(v, false, empty)) ||
         (rc = check_seq(y, false, empty)))
         return rc;
     if (q->dtype != k->dtype || q->dtype != v->dtype) return PMA_ERR_DTYPE;
     if ((rc = check_state(state_in)) || (rc = check_state(state_out))) return rc;
-    DevInfo di;
-    if ((rc = device_info(&di))) return rc;
-    if (N == 0) return PMA_OK;
-    if ((long)N * H > (1L << 30)) return PMA_ERR_ARGUMENT;
-    DecodeParams p{};
-    p.N = N;
-    p.H = H;
-    p.q = seq_of(q);
-    p.k = seq_of(k);
-    p.v = seq_of(v);
-    p.y = seqout_of(y);
-    p.lambda = lambda;
-    p.lam_sn = lambda_stride_n;
-    p.in = *state_in;
-    p.out = *state_out;
-    p.eps = eps;
-    cudaError_t e = launch_decode(p, D, q->dtype, y->dtype, reinterpret_cast<cudaStream_t>(stream));
-    return e == cudaSuccess ? PMA_OK : cuda_fail(e);
-}
-
-int pma_decode_step_rows(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
-                         const pma_seq_tensor *v, const float *lambda, int64_t lambda_stride_n, const int32_t *rows,
-                         int pool_rows, const pma_state *pool_in, const pma_state *pool_out, float eps,
-                         const pma_seq_tensor *y, pma_stream_t stream) {
-    if (N < 0 || H <= 0 || !lambda || lambda_stride_n < 0 || pool_rows < 0) return PMA_ERR_ARGUMENT;
-    if (N > 0 && !rows) return PMA_ERR_ARGUMENT;
-    if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
-    int rc;
-    const bool empty = N == 0;
-    if ((rc = check_seq(q, false, empty)) || (rc = check_seq(k, false, empty)) || (rc = check_seq(v, false, empty)) ||
-        (rc = check_seq(y, false, empty)))
-        return rc;
-    if (q->dtype != k->dtype || q->dtype != v->dtype) return PMA_ERR_DTYPE;
-    if ((rc = check_state(pool_in)) || (rc = check_state(pool_out))) return rc;
     DevInfo di;
     if ((rc = device_info(&di))) return rc;
     if (N == 0) return PMA_OK;
@@ -317,17 +423,22 @@ int pma_decode_step_rows(int N, int H, int D, const pma_seq_tensor *q, const pma
     p.q = seq_of(q);
     p.k = seq_of(k);
     p.v = seq_of(v);
+    p.pro = pro;
     p.y = seqout_of(y);
     p.lambda = lambda;
     p.lam_sn = lambda_stride_n;
-    p.in = *pool_in;
-    p.out = *pool_out;
+    p.in = *state_in;
+    p.out = *state_out;
     p.eps = eps;
     p.rows = rows;
-    p.pool_rows = pool_rows;
+    p.pool_rows = rows ? pool_rows : 0;
     cudaError_t e = launch_decode(p, D, q->dtype, y->dtype, reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? PMA_OK : cuda_fail(e);
 }
+
+}  // namespace
+
+extern "C" {
 
 int pma_state_combine(int B, int H, int D, const float *lambda, int64_t lambda_stride_b, int64_t len,
                       const pma_state *T, const pma_state *P, pma_stream_t stream) {

@@ -80,6 +80,50 @@ struct SeqOut {
     int64_t sb, sh, sl;
 };
 
+// Input prologue (pma_prologue): kv head = h / groups; q -> LN(q) * q_scale, k -> LN(k).
+struct Prologue {
+    int groups;
+    float q_scale;
+    const float *qw, *qb, *kw, *kb;   // qw / kw null: no norm; qb / kb null: zero bias
+    float ln_eps;
+    __host__ __device__ bool q_work() const { return qw != nullptr || q_scale != 1.0f; }
+    __host__ __device__ bool k_work() const { return kw != nullptr; }
+};
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
+// Mean and 1/sqrt(biased var + eps) of a D-element row, read by one warp (two passes over
+// the row: the variance is the mean of squared deviations, as nn.LayerNorm computes it).
+template <int D, typename T>
+__device__ __forceinline__ float2 warp_row_stats(const T *row, float eps, int lane) {
+    float s = 0.f;
+    for (int d = lane; d < D; d += 32) s += Elem<T>::to_f(row[d]);
+    const float mean = warp_sum(s) * (1.0f / D);
+    float v = 0.f;
+    for (int d = lane; d < D; d += 32) {
+        const float t = Elem<T>::to_f(row[d]) - mean;
+        v = fmaf(t, t, v);
+    }
+    return make_float2(mean, rsqrtf(warp_sum(v) * (1.0f / D) + eps));
+}
+
+// (x - mean) * rstd * w[d] + b[d] (w null: x), then * scale.
+__device__ __forceinline__ float prologue_elem(float x, float2 st, const float *w, const float *b, int d,
+                                              float scale) {
+    if (w) x = fmaf((x - st.x) * st.y, __ldg(w + d), b ? __ldg(b + d) : 0.f);
+    return x * scale;
+}
+
+__device__ __forceinline__ float4 prologue4(float4 x, float2 st, const float *w, const float *b, int d0,
+                                           float scale) {
+    return make_float4(prologue_elem(x.x, st, w, b, d0, scale), prologue_elem(x.y, st, w, b, d0 + 1, scale),
+                       prologue_elem(x.z, st, w, b, d0 + 2, scale), prologue_elem(x.w, st, w, b, d0 + 3, scale));
+}
+
 // Pointers to one head-state.
 struct HeadPtrs {
     float *S0, *S1, *S2, *Z0, *Z1, *Z2;

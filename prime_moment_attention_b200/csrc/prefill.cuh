@@ -11,7 +11,8 @@ namespace pma {
 struct PrefillParams {
     int B, H, L;
     int seg_len;          // multiple of the kernel's chunk
-    Seq q, k, v;
+    Seq q, k, v;          // k, v: H / pro.groups heads
+    Prologue pro;
     SeqOut y;             // y.p == nullptr: no output rows
     const float *lambda;
     int64_t lam_sb;
@@ -27,7 +28,8 @@ constexpr size_t WS_HEADER = 256;
 
 struct DecodeParams {
     int N, H;
-    Seq q, k, v;            // [N,H,D] (stride_l unused)
+    Seq q, k, v;            // [N,H,D] (stride_l unused); k, v: H / pro.groups heads
+    Prologue pro;
     SeqOut y;
     const float *lambda;
     int64_t lam_sn;
@@ -44,6 +46,11 @@ cudaError_t launch_segment_prefix(int BH, int H, int D, int nseg, int seg_len, i
                                   const StateRef &final_out, const float *lambda, int64_t lam_sb, cudaStream_t st);
 cudaError_t launch_state_combine(int B, int H, int D, const float *lambda, int64_t lam_sb, int64_t len,
                                  const pma_state &T, const pma_state &P, cudaStream_t st);
+
+// QK-norm pass for the tensor-core path: rows of src [B, Hs, L, 64] bf16 (any strides) ->
+// contiguous dst, (LN(x) if w else x) * scale.
+cudaError_t launch_qk_norm(const Seq &src, int B, int Hs, int L, const float *w, const float *b, float eps,
+                           float scale, void *dst, int sms, cudaStream_t st);
 
 // tcgen05 tensor-core prefill (bf16 inputs, D = 64).
 constexpr int TC_CHUNK = 128;

@@ -21,7 +21,8 @@ namespace pma {
 template <int D, int C>
 struct SimtSmem {
     static constexpr int floats = 2 * D * C /*Qt,Kt*/ + 2 * C * D /*Kr,Vr*/ + C * C /*Pt*/ + 2 * D * D /*S1,S2*/ +
-                                  3 * D /*S0,Z1,Z2*/ + (C + 4) /*pw*/ + 2 * C /*den,cden*/ + 4 /*Z0*/;
+                                  3 * D /*S0,Z1,Z2*/ + (C + 4) /*pw*/ + 2 * C /*den,cden*/ + 4 /*Z0*/ +
+                                  4 * C /*prologue row stats*/;
     static constexpr size_t bytes = floats * sizeof(float);
 };
 
@@ -45,6 +46,8 @@ __device__ __forceinline__ void simt_prefill_body(const PrefillParams &p, float 
     float *const den = pw + (C + 4);                     // [C]
     float *const cden = den + C;                         // [C]
     float *const Z0 = cden + C;                          // [1]
+    float2 *const qst = reinterpret_cast<float2 *>(Z0 + 4);  // [C] LayerNorm (mean, rstd) of q rows
+    float2 *const kst = qst + C;                             // [C] and of k rows
 
     const int tid = threadIdx.x;
     const int b = bh / p.H, h = bh - b * p.H;
@@ -69,13 +72,30 @@ __device__ __forceinline__ void simt_prefill_body(const PrefillParams &p, float 
     if (tid == 0) Z0[0] = has_in ? src.Z0[0] : 0.f;
 
     const TI *qb = reinterpret_cast<const TI *>(p.q.p) + b * p.q.sb + h * p.q.sh;
-    const TI *kb = reinterpret_cast<const TI *>(p.k.p) + b * p.k.sb + h * p.k.sh;
-    const TI *vb = reinterpret_cast<const TI *>(p.v.p) + b * p.v.sb + h * p.v.sh;
+    const int hk = h / p.pro.groups;  // GQA: kv head of query head h
+    const TI *kb = reinterpret_cast<const TI *>(p.k.p) + b * p.k.sb + hk * p.k.sh;
+    const TI *vb = reinterpret_cast<const TI *>(p.v.p) + b * p.v.sb + hk * p.v.sh;
+    const bool q_pro = want_y && p.pro.q_work(), q_norm = want_y && p.pro.qw, k_norm = p.pro.kw != nullptr;
     TO *yb = want_y ? reinterpret_cast<TO *>(p.y.p) + b * p.y.sb + h * p.y.sh : nullptr;
     __syncthreads();
 
     for (int t0 = t_begin; t0 < t_end; t0 += C) {
         const int n = min(C, t_end - t0);
+        // ---- prologue row statistics (one warp per token row, read from global/L2) ----
+        if (q_norm || k_norm) {
+            const int warp = tid >> 5, lane = tid & 31;
+            for (int j = warp; j < n; j += blockDim.x >> 5) {
+                if (q_norm) {
+                    const float2 st = warp_row_stats<D>(qb + (int64_t)(t0 + j) * p.q.sl, p.pro.ln_eps, lane);
+                    if (lane == 0) qst[j] = st;
+                }
+                if (k_norm) {
+                    const float2 st = warp_row_stats<D>(kb + (int64_t)(t0 + j) * p.k.sl, p.pro.ln_eps, lane);
+                    if (lane == 0) kst[j] = st;
+                }
+            }
+            __syncthreads();
+        }
         // ---- stage the chunk: transposed q/k (token index fastest across lanes) ----
         if (want_y) {
             for (int e = tid; e < C * (D / 4); e += blockDim.x) {
@@ -84,6 +104,10 @@ __device__ __forceinline__ void simt_prefill_body(const PrefillParams &p, float 
                 if (j < n) {
                     qv = load4(qb + (int64_t)(t0 + j) * p.q.sl + d0);
                     kv = load4(kb + (int64_t)(t0 + j) * p.k.sl + d0);
+                    if (q_pro)
+                        qv = prologue4(qv, q_norm ? qst[j] : make_float2(0.f, 1.f), p.pro.qw, p.pro.qb, d0,
+                                       p.pro.q_scale);
+                    if (k_norm) kv = prologue4(kv, kst[j], p.pro.kw, p.pro.kb, d0, 1.f);
                 }
                 Qt[(d0 + 0) * C + j] = qv.x; Qt[(d0 + 1) * C + j] = qv.y;
                 Qt[(d0 + 2) * C + j] = qv.z; Qt[(d0 + 3) * C + j] = qv.w;
@@ -98,6 +122,7 @@ __device__ __forceinline__ void simt_prefill_body(const PrefillParams &p, float 
             if (j < n) {
                 kv = load4(kb + (int64_t)(t0 + j) * p.k.sl + d0);
                 vv = load4(vb + (int64_t)(t0 + j) * p.v.sl + d0);
+                if (k_norm) kv = prologue4(kv, kst[j], p.pro.kw, p.pro.kb, d0, 1.f);
             }
             store4(Kr + j * D + d0, kv);
             store4(Vr + j * D + d0, vv);

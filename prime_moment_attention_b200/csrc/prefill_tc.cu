@@ -379,7 +379,10 @@ __device__ __forceinline__ void store_row32<float>(float *dst, const float *v) {
 }
 
 // ------------------------------------------------------------------ the kernel
-template <bool SO, typename TO>   // SO: state only (no q, no output rows)
+// SO: state only (no q, no output rows).  PRO: q scaled by p.pro.q_scale as the prep warps load it
+// (the host uses this only when the scale is exact in bf16, so q * scale rounds as in float32;
+// LayerNorm prologues run as a separate pass before this kernel).
+template <bool SO, typename TO, bool PRO>
 __global__ void __launch_bounds__(512, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                       const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
@@ -390,6 +393,7 @@ __global__ void __launch_bounds__(512, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.x, seg = blockIdx.y;
     const int b = bh / p.H, h = bh - b * p.H;
+    const int hk = h / p.pro.groups;  // GQA: kv head of query head h
     const float lam = p.lambda[(int64_t)b * p.lam_sb + h];
 
     if (!(lam >= LMIN)) {  // small decay (or NaN): float32 CUDA-core chunk loop, whole CTA
@@ -457,8 +461,8 @@ __global__ void __launch_bounds__(512, 1)
                 for (; fetched < U && fetched <= u + PREFETCH; ++fetched) {
                     const int tf = (c_begin + fetched) * C;
                     if (!SO) tma_prefetch_l2(&tq, 0, tf, h, b);
-                    tma_prefetch_l2(&tk, 0, tf, h, b);
-                    tma_prefetch_l2(&tv, 0, tf, h, b);
+                    tma_prefetch_l2(&tk, 0, tf, hk, b);
+                    tma_prefetch_l2(&tv, 0, tf, hk, b);
                 }
                 if (!mbar_wait(&bar[B_EMPTY0 + s], ((u / NST) & 1) ^ 1, ctl, 1)) break;
                 if (!SO && !mbar_wait(&bar[B_QEMPTY0 + (u & 1)], ((u >> 1) & 1) ^ 1, ctl, 3)) break;
@@ -466,8 +470,8 @@ __global__ void __launch_bounds__(512, 1)
                 uint8_t *base = smem + s * STAGE;
                 mbar_expect_tx(&bar[B_FULL0 + s], SO ? 2 * TILE : 3 * TILE);
                 if (!SO) tma_load(smem + OFF_Q + (u & 1) * TILE, &tq, &bar[B_FULL0 + s], 0, t0, h, b);
-                tma_load(base + OFF_K, &tk, &bar[B_FULL0 + s], 0, t0, h, b);
-                tma_load(base + OFF_V, &tv, &bar[B_FULL0 + s], 0, t0, h, b);
+                tma_load(base + OFF_K, &tk, &bar[B_FULL0 + s], 0, t0, hk, b);
+                tma_load(base + OFF_V, &tv, &bar[B_FULL0 + s], 0, t0, hk, b);
                 issued = u + 1;
             }
             // never leave with copies in flight: the last (up to) NST stages must have landed
@@ -653,6 +657,13 @@ __global__ void __launch_bounds__(512, 1)
                 float4 *pp = reinterpret_cast<float4 *>(sm.part[s][wp]) + cc * 2;
                 pp[0] = make_float4(s0p[0].x, s0p[0].y, s0p[1].x, s0p[1].y);
                 pp[1] = make_float4(s0p[2].x, s0p[2].y, s0p[3].x, s0p[3].y);
+            }
+            if (PRO && !SO) {  // q * scale in bf16 (exact scale: one rounding, as in float32)
+                const __nv_bfloat162 sc = __float2bfloat162_rn(p.pro.q_scale);
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    xq[c] = make_uint4(as_u(__hmul2(as_b2(xq[c].x), sc)), as_u(__hmul2(as_b2(xq[c].y), sc)),
+                                       as_u(__hmul2(as_b2(xq[c].z), sc)), as_u(__hmul2(as_b2(xq[c].w), sc)));
             }
             // QQ row tid: [q | q^2/2], 2 bf16 per tensor-memory column, once the carry GEMM of chunk
             // u-2 has finished reading this buffer
@@ -977,11 +988,11 @@ static bool make_map(CUtensorMap *m, const Seq &s, int B, int H, int L) {
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool SO, typename TO>
+template <bool SO, typename TO, bool PRO>
 static cudaError_t launch_t(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
                             const PrefillParams &p, dim3 grid, cudaStream_t st) {
-    auto kern = prefill_tc_kernel<SO, TO>;
-    cudaError_t e = set_smem_once<prefill_tc_kernel<SO, TO>>((int)SMEM_BYTES);
+    auto kern = prefill_tc_kernel<SO, TO, PRO>;
+    cudaError_t e = set_smem_once<prefill_tc_kernel<SO, TO, PRO>>((int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     kern<<<grid, 512, SMEM_BYTES, st>>>(mq, mk, mv, p);
     return cudaGetLastError();
@@ -993,16 +1004,21 @@ bool tc_supported(int D, int idt) { return D == 64 && idt == PMA_BF16 && tc::get
 
 cudaError_t launch_prefill_tc(const PrefillParams &p, int ydt, dim3 grid, cudaStream_t st) {
     CUtensorMap mq, mk, mv;
-    if (!tc::make_map(&mk, p.k, p.B, p.H, p.L) || !tc::make_map(&mv, p.v, p.B, p.H, p.L)) return cudaErrorInvalidValue;
+    const int hkv = p.H / p.pro.groups;
+    if (!tc::make_map(&mk, p.k, p.B, hkv, p.L) || !tc::make_map(&mv, p.v, p.B, hkv, p.L)) return cudaErrorInvalidValue;
     if (!p.state_only && p.y.p) {
         if (!tc::make_map(&mq, p.q, p.B, p.H, p.L)) return cudaErrorInvalidValue;
     } else {
         mq = mk;
     }
     const bool so = p.state_only || !p.y.p;
-    if (so) return tc::launch_t<true, float>(mq, mk, mv, p, grid, st);
-    return ydt == PMA_F32 ? tc::launch_t<false, float>(mq, mk, mv, p, grid, st)
-                          : tc::launch_t<false, __nv_bfloat16>(mq, mk, mv, p, grid, st);
+    if (p.pro.qw || p.pro.kw) return cudaErrorInvalidValue;  // norms are applied by the prologue pass
+    if (so) return tc::launch_t<true, float, false>(mq, mk, mv, p, grid, st);
+    if (p.pro.q_scale != 1.0f)
+        return ydt == PMA_F32 ? tc::launch_t<false, float, true>(mq, mk, mv, p, grid, st)
+                              : tc::launch_t<false, __nv_bfloat16, true>(mq, mk, mv, p, grid, st);
+    return ydt == PMA_F32 ? tc::launch_t<false, float, false>(mq, mk, mv, p, grid, st)
+                          : tc::launch_t<false, __nv_bfloat16, false>(mq, mk, mv, p, grid, st);
 }
 
 }  // namespace pma

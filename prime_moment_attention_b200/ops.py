@@ -9,6 +9,7 @@ State tuples use the reference layout (src/prime_moment_attention/attention.py:1
 from __future__ import annotations
 
 import ctypes
+from dataclasses import dataclass
 from typing import Optional, Sequence, Tuple, Union
 
 import torch
@@ -109,6 +110,47 @@ def lambda_tensor(decay: Decay, B: int, H: int, device) -> Tuple[torch.Tensor, i
     raise ValueError(f"decay must be a scalar, [H] or [B,H]; got shape {tuple(lam.shape)}")
 
 
+@dataclass
+class Prologue:
+    """Module work between the projections and the core, folded into the kernels' loads
+    (pma_prologue): k and v carry H / kv_groups heads and query head h reads kv head
+    h // kv_groups (the reference's repeat_interleave, attention.py:92-94); q and k get a
+    LayerNorm over the head dim when their weight is given (attention.py:96-98); q is then
+    multiplied by q_scale (attention.py:101).  Weights and biases are [D] tensors."""
+    kv_groups: int = 1
+    q_scale: float = 1.0
+    q_norm_weight: Optional[torch.Tensor] = None
+    q_norm_bias: Optional[torch.Tensor] = None
+    k_norm_weight: Optional[torch.Tensor] = None
+    k_norm_bias: Optional[torch.Tensor] = None
+    norm_eps: float = 1e-5
+
+    def to_c(self, D: int, device) -> Tuple[_lib.Prologue, list]:
+        """The C struct and the float32 device tensors it points to (keep them alive)."""
+        keep = []
+
+        def ptr(t):
+            if t is None:
+                return None
+            if t.numel() != D:
+                raise ValueError(f"prologue norm parameters must have head_dim={D} elements")
+            if t.device != device or t.dtype != torch.float32 or not t.is_contiguous():
+                t = t.detach().to(device=device, dtype=torch.float32).contiguous()
+            keep.append(t)
+            return t.data_ptr()
+
+        c = _lib.Prologue(int(self.kv_groups), float(self.q_scale), ptr(self.q_norm_weight), ptr(self.q_norm_bias),
+                          ptr(self.k_norm_weight), ptr(self.k_norm_bias), float(self.norm_eps))
+        return c, keep
+
+
+def _kv_heads(H: int, prologue: Optional[Prologue]) -> int:
+    g = 1 if prologue is None else int(prologue.kv_groups)
+    if g < 1 or H % g:
+        raise ValueError(f"kv_groups={g} must be a positive divisor of num_heads={H}")
+    return H // g
+
+
 def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -116,20 +158,25 @@ def _stream(device) -> int:
 def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
             state: Optional[StateTuple] = None, eps: float = 1.0, return_state: bool = True,
             out_dtype: Optional[torch.dtype] = None, y_out: Optional[torch.Tensor] = None,
-            want_y: bool = True, check: bool = False):
+            want_y: bool = True, check: bool = False, prologue: Optional[Prologue] = None):
     """Chunked prefill over q, k, v [B,H,L,D] (q pre-scaled by 1/sqrt(D)).
 
     Returns (y [B,H,L,D] or None, final state or None).  `y_out` may be a
     preallocated [B,H,L,D] view with any strides (e.g. a transpose of [B,L,H,D]).
     `want_y=False` runs the state-only pass.  `check=True` synchronises and raises
-    if the kernel recorded a failure in its status word (a bounded wait expired)."""
+    if the kernel recorded a failure in its status word (a bounded wait expired).
+    With a `prologue`, q, k, v are the raw projections (k, v with H / kv_groups heads)
+    and the kernels apply the GQA map, QK-norm and q scale as they load them."""
     dev = _require_cuda(q, k, v)
-    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
-        raise ValueError(f"q, k, v must share one [B,H,L,D] shape; got {tuple(q.shape)}, {tuple(k.shape)}, "
-                         f"{tuple(v.shape)}")
+    if q.dim() != 4:
+        raise ValueError(f"q must be [B,H,L,D]; got {tuple(q.shape)}")
+    B, H, L, D = q.shape
+    kv_shape = (B, _kv_heads(H, prologue), L, D)
+    if tuple(k.shape) != kv_shape or tuple(v.shape) != kv_shape:
+        raise ValueError(f"q, k, v must be [B,H,L,D] and [B,H/kv_groups,L,D]; got {tuple(q.shape)}, "
+                         f"{tuple(k.shape)}, {tuple(v.shape)}")
     if k.dtype != q.dtype or v.dtype != q.dtype:
         raise TypeError("q, k, v must share one dtype")
-    B, H, L, D = q.shape
     L_ = _lib.load()
     qs, q = _seq(q)
     ks, k = _seq(k)
@@ -152,12 +199,21 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
             y = torch.empty(B, H, L, D, dtype=out_dtype or q.dtype, device=dev)
         ys_c, _ = _seq(y)
         ys = ctypes.byref(ys_c)
-    ws_bytes = L_.pma_prefill_workspace_bytes(B, H, L, D, _DT[q.dtype])
+    if prologue is None:
+        ws_bytes = L_.pma_prefill_workspace_bytes(B, H, L, D, _DT[q.dtype])
+    else:
+        pc, keep = prologue.to_c(D, dev)
+        ws_bytes = L_.pma_prefill_ex_workspace_bytes(B, H, L, D, _DT[q.dtype], ctypes.byref(pc))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
-    rc = L_.pma_prefill(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(), lam_sb,
-                        st_in, st_out, float(eps), ys, ws.data_ptr() if ws is not None else None, ws_bytes,
-                        _stream(dev))
-    _lib.check("pma_prefill", rc)
+    wsp = ws.data_ptr() if ws is not None else None
+    if prologue is None:
+        rc = L_.pma_prefill(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(),
+                            lam_sb, st_in, st_out, float(eps), ys, wsp, ws_bytes, _stream(dev))
+        _lib.check("pma_prefill", rc)
+    else:
+        rc = L_.pma_prefill_ex(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), ctypes.byref(pc),
+                               lam.data_ptr(), lam_sb, st_in, st_out, float(eps), ys, wsp, ws_bytes, _stream(dev))
+        _lib.check("pma_prefill_ex", rc)
     if check and ws is not None:
         code = int(ws[:4].view(torch.int32).item())
         if code != 0:
@@ -167,16 +223,15 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
 
 def decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay, state: StateTuple,
                 eps: float = 1.0, inplace: bool = False, out_dtype: Optional[torch.dtype] = None,
-                y_out: Optional[torch.Tensor] = None):
+                y_out: Optional[torch.Tensor] = None, prologue: Optional[Prologue] = None):
     """One recurrent step: q, k, v [N,H,D] -> (y [N,H,D], new state).
 
     With inplace=True the given state tensors are updated and returned (they must
     already be contiguous float32); otherwise fresh tensors are returned and the
-    input state is left untouched, as in the reference (attention.py:126-132)."""
+    input state is left untouched, as in the reference (attention.py:126-132).
+    `prologue` as in prefill (k, v then [N, H / kv_groups, D])."""
     dev = _require_cuda(q, k, v)
-    if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
-        raise ValueError("q, k, v must share one [N,H,D] shape")
-    N, H, D = q.shape
+    N, H, D = _check_step_shapes(q, k, v, prologue)
     L_ = _lib.load()
     qs, q = _seq(q, False)
     ks, k = _seq(k, False)
@@ -195,25 +250,41 @@ def decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
     ys, y2 = _seq(y, False)
     if y2 is not y:
         raise ValueError("y_out must have a contiguous, 16-byte aligned last axis")
-    rc = L_.pma_decode_step(N, H, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(), lam_sn,
-                            ctypes.byref(st_in_c), ctypes.byref(st_out_c), float(eps), ctypes.byref(ys),
-                            _stream(dev))
-    _lib.check("pma_decode_step", rc)
+    if prologue is None:
+        rc = L_.pma_decode_step(N, H, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(),
+                                lam_sn, ctypes.byref(st_in_c), ctypes.byref(st_out_c), float(eps), ctypes.byref(ys),
+                                _stream(dev))
+        _lib.check("pma_decode_step", rc)
+    else:
+        pc, keep = prologue.to_c(D, dev)
+        rc = L_.pma_decode_step_ex(N, H, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), ctypes.byref(pc),
+                                   lam.data_ptr(), lam_sn, None, 0, ctypes.byref(st_in_c), ctypes.byref(st_out_c),
+                                   float(eps), ctypes.byref(ys), _stream(dev))
+        _lib.check("pma_decode_step_ex", rc)
     return y, st_out_t
+
+
+def _check_step_shapes(q, k, v, prologue):
+    if q.dim() != 3:
+        raise ValueError("q must be [N,H,D]")
+    N, H, D = q.shape
+    kv_shape = (N, _kv_heads(H, prologue), D)
+    if tuple(k.shape) != kv_shape or tuple(v.shape) != kv_shape:
+        raise ValueError(f"q, k, v must be [N,H,D] and [N,H/kv_groups,D]; got {tuple(q.shape)}, {tuple(k.shape)}, "
+                         f"{tuple(v.shape)}")
+    return N, H, D
 
 
 def decode_step_rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay, pool: StateTuple,
                      rows: torch.Tensor, eps: float = 1.0, out_dtype: Optional[torch.dtype] = None,
-                     y_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     y_out: Optional[torch.Tensor] = None, prologue: Optional[Prologue] = None) -> torch.Tensor:
     """One recurrent step for batch rows n = 0..N-1 whose states are rows rows[n] of `pool`.
 
     `pool` is a state tuple [P, H, ...] (contiguous float32, updated in place); `rows` an int32
     CUDA tensor [N] of pool rows (rows outside [0, P) are skipped and their y rows untouched).
-    Returns y [N, H, D]."""
+    `prologue` as in prefill.  Returns y [N, H, D]."""
     dev = _require_cuda(q, k, v)
-    if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
-        raise ValueError("q, k, v must share one [N,H,D] shape")
-    N, H, D = q.shape
+    N, H, D = _check_step_shapes(q, k, v, prologue)
     P = pool[0].shape[0]
     if rows.dtype != torch.int32 or rows.dim() != 1 or rows.shape[0] != N or rows.device != dev:
         raise ValueError("rows must be an int32 tensor [N] on the inputs' device")
@@ -230,10 +301,17 @@ def decode_step_rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: D
     ys, y2 = _seq(y, False)
     if y2 is not y:
         raise ValueError("y_out must have a contiguous, 16-byte aligned last axis")
-    rc = L_.pma_decode_step_rows(N, H, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(), lam_sn,
-                                 rows.data_ptr(), P, ctypes.byref(pool_c), ctypes.byref(pool_c), float(eps),
-                                 ctypes.byref(ys), _stream(dev))
-    _lib.check("pma_decode_step_rows", rc)
+    if prologue is None:
+        rc = L_.pma_decode_step_rows(N, H, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(),
+                                     lam_sn, rows.data_ptr(), P, ctypes.byref(pool_c), ctypes.byref(pool_c),
+                                     float(eps), ctypes.byref(ys), _stream(dev))
+        _lib.check("pma_decode_step_rows", rc)
+    else:
+        pc, keep = prologue.to_c(D, dev)
+        rc = L_.pma_decode_step_ex(N, H, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), ctypes.byref(pc),
+                                   lam.data_ptr(), lam_sn, rows.data_ptr(), P, ctypes.byref(pool_c),
+                                   ctypes.byref(pool_c), float(eps), ctypes.byref(ys), _stream(dev))
+        _lib.check("pma_decode_step_ex", rc)
     return y
 
 
