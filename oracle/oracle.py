@@ -41,6 +41,11 @@ def lib() -> ctypes.CDLL:
         L.orc_prefill.restype = ctypes.c_int
         L.orc_combine.argtypes = [ctypes.c_int, ctypes.c_double, ctypes.c_long, _dp, _dp]
         L.orc_combine.restype = None
+        L.orc_delta_prefill.argtypes = ([ctypes.c_int] * 4 + [_dp] * 6 + [ctypes.c_int, ctypes.c_double,
+                                        ctypes.c_double] + [_dp] * 3)
+        L.orc_delta_prefill.restype = ctypes.c_int
+        L.orc_delta_step.argtypes = [ctypes.c_int] * 3 + [_dp] * 5 + [ctypes.c_double] * 2 + [_dp] * 3
+        L.orc_delta_step.restype = ctypes.c_int
         _LIB = L
     return _LIB
 
@@ -121,3 +126,45 @@ def rel_err(a, b) -> float:
     if den == 0.0:
         return num
     return num / den
+
+
+def delta_prefill(q, k, v, beta, alpha, lam, chunk: int = 64, bound: float = 25.0, norm_eps: float = 1e-5,
+                  state=None, want_y: bool = True):
+    """Gated delta-rule chunked prefill (chunked_delta_prime.py:175-283) as a token recurrence.
+
+    q (pre-scaled), k, v [B,H,L,D]; beta, alpha [B,H,L] (alpha None: alpha_t = lam[h]); lam [H]
+    (the decay of padded tokens); state [B,H,D,2D] or None.  Returns (y [B,H,L,D], state)."""
+    q, k, v = _f64(q), _f64(k), _f64(v)
+    B, H, L, D = q.shape
+    beta = _f64(beta).reshape(B, H, L)
+    al = None if alpha is None else np.ascontiguousarray(_f64(alpha).reshape(B, H, L))
+    lt = _f64(lam).reshape(-1)
+    if lt.size == 1:
+        lt = np.full(H, float(lt[0]))
+    st_in = None if state is None else np.ascontiguousarray(_f64(state).reshape(B, H, D, 2 * D))
+    st = np.zeros((B, H, D, 2 * D))
+    y = np.zeros_like(q) if want_y else None
+    rc = lib().orc_delta_prefill(B, H, L, D, _ptr(q), _ptr(k), _ptr(v), _ptr(beta),
+                                 _ptr(al) if al is not None else None, _ptr(lt), int(chunk), float(bound),
+                                 float(norm_eps), _ptr(st_in) if st_in is not None else None, _ptr(st),
+                                 _ptr(y) if y is not None else None)
+    if rc != 0:
+        raise ValueError("orc_delta_prefill rejected its arguments")
+    return y, st
+
+
+def delta_step(q, k, v, beta, alpha, state, bound: float = 25.0, norm_eps: float = 1e-5):
+    """Gated delta-rule L == 1 step (chunked_delta_prime.py:142-172): q, k, v [N,H,D], beta,
+    alpha [N,H], state [N,H,D,2D].  Returns (y [N,H,D], new state)."""
+    q, k, v = _f64(q), _f64(k), _f64(v)
+    N, H, D = q.shape
+    beta = np.ascontiguousarray(_f64(beta).reshape(N, H))
+    alpha = np.ascontiguousarray(_f64(alpha).reshape(N, H))
+    st_in = np.ascontiguousarray(_f64(state).reshape(N, H, D, 2 * D))
+    st = np.zeros_like(st_in)
+    y = np.zeros_like(q)
+    rc = lib().orc_delta_step(N, H, D, _ptr(q), _ptr(k), _ptr(v), _ptr(beta), _ptr(alpha), float(bound),
+                              float(norm_eps), _ptr(st_in), _ptr(st), _ptr(y))
+    if rc != 0:
+        raise ValueError("orc_delta_step rejected its arguments")
+    return y, st

@@ -31,6 +31,9 @@
  *                     chunked core mishandles (chunked_ssd.py:129-137 broadcasts
  *                     [B,H,1,D] against [1,1,nc,1,1]).
  *
+ *   orc_delta_prefill / orc_delta_step   the gated delta-rule variant (see the
+ *                     section at the end of this file).
+ *
  * Extension over the reference: lambda may differ per head (and per batch row).
  * The reference holds one scalar decay per module (attention.py:49); heads are
  * independent, so the per-head result equals the reference run once per head
@@ -139,4 +142,145 @@ void orc_combine(int F, double lam, long len, double *P, const double *T)
 {
     const double a = pow(lam, (double)len);
     for (int i = 0; i < F; ++i) P[i] = a * P[i] + T[i];
+}
+
+/* ---------------------------------------------------------------------------
+ * Gated delta-rule variant: ChunkedGatedDeltaPrimeAttention
+ * (src/prime_moment_attention/chunked_delta_prime.py).  One head has a state
+ * S [D][2D] (row = value index d, column = feature index f) and per token the
+ * features (:73-87)
+ *     psi = [q, q^2 / sqrt 2]
+ *     phi = [k / max(|k|, e), (k^2 / max(|k^2|, e)) / sqrt 2]
+ * with gates beta_t (write) and alpha_t (retention), given per token.
+ *
+ * orc_delta_prefill: the chunked prefill (:175-283).  Its per-chunk solve
+ *     T E = u,  T = I + strict_tril(Lambda * (Phi Phi^T) * beta_j),
+ *     u_i = v_i - exp(cum_i) S phi_i,  cum_i = sum_{t<=i} log alpha_t
+ * is, row by row, the token recurrence
+ *     e_i = v_i - alpha_i S phi_i            (error against the decayed state)
+ *     S   = alpha_i S + beta_i e_i phi_i^T
+ *     y_i = S psi_i
+ * (E_i = e_i; the readout y_intra + y_inter of :248-255 is S_i psi_i), which
+ * is what this function iterates.  alpha is used as clamp(alpha, 1e-5, 1)
+ * (the log of :197).  At the end of every chunk of `chunk` tokens counted from
+ * the start of the call the Lyapunov projection (:267-270)
+ *     S *= min(1, bound / (|S|_F + 1e-6))          (bound <= 0: off)
+ * is applied.  A ragged last chunk is padded (:178-185) with zero features,
+ * zero beta and alpha = the module's decay, so the final state is further
+ * multiplied by decay^pad before that chunk's projection; `lam` is that decay
+ * (one per head here: the reference module holds one scalar).
+ *
+ * orc_delta_step: the L == 1 branch (:142-172), which differs from the prefill:
+ *     e = v - S phi   (error against the undecayed state)
+ *     S = alpha S + beta e phi^T;  Lyapunov projection every step;  y = S psi.
+ *
+ * Layouts: q,k,v,y [B,H,L,D]; beta, alpha [B,H,L]; lam [H]; state [B,H,D,2D].
+ * state_in may be NULL (zero); state_out receives the final state.
+ * ------------------------------------------------------------------------- */
+static void delta_features(int D, const double *q, const double *k, double ne, double *psi, double *phi)
+{
+    const double r2 = 1.0 / sqrt(2.0);
+    double n1 = 0.0, n2 = 0.0;
+    for (int d = 0; d < D; ++d) {
+        n1 += k[d] * k[d];
+        n2 += k[d] * k[d] * k[d] * k[d];
+    }
+    n1 = sqrt(n1);
+    n2 = sqrt(n2);
+    if (n1 < ne) n1 = ne;
+    if (n2 < ne) n2 = ne;
+    for (int d = 0; d < D; ++d) {
+        phi[d] = k[d] / n1;
+        phi[D + d] = k[d] * k[d] / n2 * r2;
+        psi[d] = q[d];
+        psi[D + d] = q[d] * q[d] * r2;
+    }
+}
+
+static void delta_lyapunov(int n, double bound, double *S)
+{
+    if (!(bound > 0.0)) return;
+    double s = 0.0;
+    for (int i = 0; i < n; ++i) s += S[i] * S[i];
+    double sc = bound / (sqrt(s) + 1e-6);
+    if (sc > 1.0) sc = 1.0;
+    for (int i = 0; i < n; ++i) S[i] *= sc;
+}
+
+/* one token: err_decayed = 1 for the prefill's error, 0 for the step's */
+static void delta_token(int D, const double *q, const double *k, const double *v, double beta, double alpha,
+                        double ne, int err_decayed, double *S, double *psi, double *phi)
+{
+    const int F = 2 * D;
+    delta_features(D, q, k, ne, psi, phi);
+    for (int d = 0; d < D; ++d) {
+        double *row = S + (size_t)d * F;
+        double sp = 0.0;
+        for (int f = 0; f < F; ++f) sp += row[f] * phi[f];
+        const double e = v[d] - (err_decayed ? alpha : 1.0) * sp;
+        for (int f = 0; f < F; ++f) row[f] = alpha * row[f] + beta * e * phi[f];
+    }
+}
+
+static void delta_readout(int D, const double *S, const double *psi, double *y)
+{
+    const int F = 2 * D;
+    for (int d = 0; d < D; ++d) {
+        double acc = 0.0;
+        for (int f = 0; f < F; ++f) acc += S[(size_t)d * F + f] * psi[f];
+        y[d] = acc;
+    }
+}
+
+int orc_delta_prefill(int B, int H, int L, int D, const double *q, const double *k, const double *v,
+                      const double *beta, const double *alpha, const double *lam, int chunk, double bound,
+                      double norm_eps, const double *state_in, double *state_out, double *y)
+{
+    if (B < 0 || H <= 0 || L < 0 || D <= 0 || D > 256 || chunk <= 0 || !lam || !state_out) return ORC_EINVAL;
+    const int F = 2 * D;
+    const size_t SZ = (size_t)D * F;
+    double psi[512], phi[512];
+    for (int b = 0; b < B; ++b)
+        for (int h = 0; h < H; ++h) {
+            const size_t i = (size_t)b * H + h;
+            double *S = state_out + i * SZ;
+            if (state_in) memcpy(S, state_in + i * SZ, SZ * sizeof(double));
+            else memset(S, 0, SZ * sizeof(double));
+            for (int t = 0; t < L; ++t) {
+                const size_t o = (i * (size_t)L + t) * D, g = i * (size_t)L + t;
+                double a = alpha ? alpha[g] : lam[h];
+                if (a < 1e-5) a = 1e-5;
+                if (a > 1.0) a = 1.0;
+                delta_token(D, q + o, k + o, v + o, beta[g], a, norm_eps, 1, S, psi, phi);
+                if (y) delta_readout(D, S, psi, y + o);
+                if ((t + 1) % chunk == 0) delta_lyapunov((int)SZ, bound, S);
+            }
+            if (L % chunk) {
+                double lp = lam[h];
+                if (lp < 1e-5) lp = 1e-5;
+                if (lp > 1.0) lp = 1.0;
+                const double f = pow(lp, (double)(chunk - L % chunk));
+                for (size_t j = 0; j < SZ; ++j) S[j] *= f;
+                delta_lyapunov((int)SZ, bound, S);
+            }
+        }
+    return ORC_OK;
+}
+
+int orc_delta_step(int N, int H, int D, const double *q, const double *k, const double *v, const double *beta,
+                   const double *alpha, double bound, double norm_eps, const double *state_in, double *state_out,
+                   double *y)
+{
+    if (N < 0 || H <= 0 || D <= 0 || D > 256 || !state_in || !state_out || !alpha || !beta) return ORC_EINVAL;
+    const int F = 2 * D;
+    const size_t SZ = (size_t)D * F;
+    double psi[512], phi[512];
+    for (size_t i = 0; i < (size_t)N * H; ++i) {
+        double *S = state_out + i * SZ;
+        if (S != state_in + i * SZ) memcpy(S, state_in + i * SZ, SZ * sizeof(double));
+        delta_token(D, q + i * D, k + i * D, v + i * D, beta[i], alpha[i], norm_eps, 0, S, psi, phi);
+        delta_lyapunov((int)SZ, bound, S);
+        if (y) delta_readout(D, S, psi, y + i * D);
+    }
+    return ORC_OK;
 }
