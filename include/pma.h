@@ -279,6 +279,55 @@ PMA_API int pma_decode_step_ex(int N, int H, int D,
                                float eps, const pma_seq_tensor *y, pma_stream_t stream);
 
 /*
+ * Gated delta-rule variant (ChunkedGatedDeltaPrimeAttention,
+ * src/prime_moment_attention/chunked_delta_prime.py:25-283).  Per head-state the state is
+ * S [D][2D] float32 (row = value index, column = feature), contiguous, B x H head-states.
+ * Features per token (:73-87): psi = [q, q^2/sqrt 2], phi = [k/max(|k|,e), (k^2/max(|k^2|,e))/sqrt 2]
+ * with e = norm_eps (the module's eps, 1e-5).  beta (write rate) and alpha (retention) are
+ * per token: the module's beta = mean(sigmoid(write_proj))/2 and
+ * alpha = decay * (1 - mean(sigmoid(erase_proj))/2) (:134-137).
+ */
+
+/*
+ * Chunked delta-rule prefill (:175-283).  Replaces the L > 1 branch of
+ * ChunkedGatedDeltaPrimeAttention.forward after the projections and gates.
+ *
+ *   q, k, v     [B,H,L,D] (F32 or BF16, same dtype; q pre-scaled by 1/sqrt(D)); D in {16, 32, 64}.
+ *   beta        device float [B,H,L] contiguous.
+ *   alpha       device float [B,H,L] contiguous, or NULL: alpha_t = lambda of the head.
+ *   lambda      lambda[b * lambda_stride_b + h]: the module's decay, used for the padded tokens
+ *               of a ragged last chunk (the reference pads alpha with it, so the final state
+ *               carries decay^pad, :178-185) and as alpha when alpha is NULL.
+ *   chunk       the reference's chunk_size (32 or 64): the Lyapunov projection
+ *               S *= min(1, bound / (|S|_F + 1e-6)) runs at every chunk end (:267-270);
+ *               lyapunov_bound <= 0 turns it off.
+ *   state_in    [B,H,D,2D] or NULL (zero); state_out [B,H,D,2D] or NULL; they may alias.
+ *   y           [B,H,L,D] (F32 or BF16) or NULL (state only; then state_out is required).
+ * Computed in float32 on CUDA cores (one CTA per head-state, state in shared memory).
+ */
+PMA_API int pma_delta_prefill(int B, int H, int L, int D,
+                              const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                              const float *beta, const float *alpha,
+                              const float *lambda, int64_t lambda_stride_b,
+                              int chunk, float lyapunov_bound, float norm_eps,
+                              const float *state_in, float *state_out,
+                              const pma_seq_tensor *y, pma_stream_t stream);
+
+/*
+ * Delta-rule decode step: the L == 1 branch (:142-172), which measures the error against the
+ * undecayed state:  e = v - S phi;  S = alpha S + beta e phi^T;  Lyapunov projection;  y = S psi.
+ *   q, k, v, y  [N,H,D] (pma_seq_tensor with L = 1); beta, alpha device float [N,H].
+ *   state_in, state_out  [N,H,D,2D]; may be the same arrays (in place).
+ * One HBM read and one write of each state.
+ */
+PMA_API int pma_delta_decode_step(int N, int H, int D,
+                                  const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                                  const float *beta, const float *alpha,
+                                  float lyapunov_bound, float norm_eps,
+                                  const float *state_in, float *state_out,
+                                  const pma_seq_tensor *y, pma_stream_t stream);
+
+/*
  * Segment carry: P <- lambda^len * P + T for B x H head-states, elementwise over
  * all six components.  len = tokens in the segment that produced T.
  * This is the associative step of the reference's inter-chunk scan

@@ -440,6 +440,90 @@ int decode_impl(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tens
 
 extern "C" {
 
+int pma_delta_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                      const pma_seq_tensor *v, const float *beta, const float *alpha, const float *lambda,
+                      int64_t lambda_stride_b, int chunk, float lyapunov_bound, float norm_eps,
+                      const float *state_in, float *state_out, const pma_seq_tensor *y, pma_stream_t stream) {
+    if (B < 0 || H <= 0 || L < 0 || !lambda || lambda_stride_b < 0 || !(norm_eps > 0.0f)) return PMA_ERR_ARGUMENT;
+    if (D != 16 && D != 32 && D != 64) return PMA_ERR_HEAD_DIM;
+    if (chunk != 32 && chunk != 64) return PMA_ERR_ARGUMENT;
+    if (!y && !state_out) return PMA_ERR_ARGUMENT;
+    int rc;
+    const bool empty = (L == 0 || B == 0);
+    if ((rc = check_seq(q, true, empty)) || (rc = check_seq(k, true, empty)) || (rc = check_seq(v, true, empty)))
+        return rc;
+    if (q->dtype != k->dtype || q->dtype != v->dtype) return PMA_ERR_DTYPE;
+    if (y && (rc = check_seq(y, true, empty))) return rc;
+    if (!empty && !beta) return PMA_ERR_ARGUMENT;
+    if ((uintptr_t)state_in % 16 || (uintptr_t)state_out % 16) return PMA_ERR_LAYOUT;
+    DevInfo di;
+    if ((rc = device_info(&di))) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const size_t sbytes = (size_t)B * H * D * 2 * D * sizeof(float);
+    if (B == 0) return PMA_OK;
+    if (L == 0) {
+        if (!state_out) return PMA_OK;
+        cudaError_t e = state_in ? (state_in == state_out ? cudaSuccess
+                                                          : cudaMemcpyAsync(state_out, state_in, sbytes,
+                                                                            cudaMemcpyDeviceToDevice, st))
+                                 : cudaMemsetAsync(state_out, 0, sbytes, st);
+        return e == cudaSuccess ? PMA_OK : cuda_fail(e);
+    }
+    DeltaParams p{};
+    p.B = B;
+    p.H = H;
+    p.L = L;
+    p.q = seq_of(q);
+    p.k = seq_of(k);
+    p.v = seq_of(v);
+    p.y = seqout_of(y);
+    p.beta = beta;
+    p.alpha = alpha;
+    p.lambda = lambda;
+    p.lam_sb = lambda_stride_b;
+    p.bound = lyapunov_bound;
+    p.norm_eps = norm_eps;
+    p.state_in = state_in;
+    p.state_out = state_out;
+    cudaError_t e = launch_delta_prefill(p, D, chunk, q->dtype, y ? y->dtype : PMA_F32, st);
+    return e == cudaSuccess ? PMA_OK : cuda_fail(e);
+}
+
+int pma_delta_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                          const pma_seq_tensor *v, const float *beta, const float *alpha, float lyapunov_bound,
+                          float norm_eps, const float *state_in, float *state_out, const pma_seq_tensor *y,
+                          pma_stream_t stream) {
+    if (N < 0 || H <= 0 || !(norm_eps > 0.0f)) return PMA_ERR_ARGUMENT;
+    if (D != 16 && D != 32 && D != 64) return PMA_ERR_HEAD_DIM;
+    int rc;
+    const bool empty = N == 0;
+    if ((rc = check_seq(q, false, empty)) || (rc = check_seq(k, false, empty)) || (rc = check_seq(v, false, empty)) ||
+        (rc = check_seq(y, false, empty)))
+        return rc;
+    if (q->dtype != k->dtype || q->dtype != v->dtype) return PMA_ERR_DTYPE;
+    if (!empty && (!beta || !alpha || !state_in || !state_out)) return PMA_ERR_ARGUMENT;
+    if ((uintptr_t)state_in % 16 || (uintptr_t)state_out % 16) return PMA_ERR_LAYOUT;
+    DevInfo di;
+    if ((rc = device_info(&di))) return rc;
+    if (N == 0) return PMA_OK;
+    if ((long)N * H > (1L << 30)) return PMA_ERR_ARGUMENT;
+    DeltaStepParams p{};
+    p.N = N;
+    p.H = H;
+    p.q = seq_of(q);
+    p.k = seq_of(k);
+    p.v = seq_of(v);
+    p.y = seqout_of(y);
+    p.beta = beta;
+    p.alpha = alpha;
+    p.bound = lyapunov_bound;
+    p.norm_eps = norm_eps;
+    p.state_in = state_in;
+    p.state_out = state_out;
+    cudaError_t e = launch_delta_step(p, D, q->dtype, y->dtype, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? PMA_OK : cuda_fail(e);
+}
+
 int pma_state_combine(int B, int H, int D, const float *lambda, int64_t lambda_stride_b, int64_t len,
                       const pma_state *T, const pma_state *P, pma_stream_t stream) {
     if (B < 0 || H <= 0 || !lambda || lambda_stride_b < 0 || len < 0) return PMA_ERR_ARGUMENT;

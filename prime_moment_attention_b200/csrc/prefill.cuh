@@ -39,6 +39,32 @@ struct DecodeParams {
     int pool_rows;          // rows in the pool (bounds for `rows`)
 };
 
+// Gated delta-rule variant (delta.cu).  State per head-state: S [D][2D] float32, row-major.
+struct DeltaParams {
+    int B, H, L;
+    Seq q, k, v;
+    SeqOut y;                 // y.p == nullptr: state only
+    const float *beta;        // [B*H*L]
+    const float *alpha;       // [B*H*L] or nullptr (alpha_t = lambda)
+    const float *lambda;      // lambda[b * lam_sb + h]: decay of padded tokens (and alpha when absent)
+    int64_t lam_sb;
+    float bound, norm_eps;
+    const float *state_in;    // [B*H][D][2D] or nullptr (zero)
+    float *state_out;         // [B*H][D][2D] or nullptr
+};
+struct DeltaStepParams {
+    int N, H;
+    Seq q, k, v;
+    SeqOut y;
+    const float *beta, *alpha;  // [N*H]
+    float bound, norm_eps;
+    const float *state_in;
+    float *state_out;
+};
+bool delta_supported(int D, int chunk);
+cudaError_t launch_delta_prefill(const DeltaParams &p, int D, int chunk, int idt, int ydt, cudaStream_t st);
+cudaError_t launch_delta_step(const DeltaStepParams &p, int D, int idt, int ydt, cudaStream_t st);
+
 cudaError_t launch_decode(const DecodeParams &p, int D, int idt, int ydt, cudaStream_t s);
 cudaError_t launch_prefill_simt(const PrefillParams &p, int D, int idt, int ydt, dim3 grid, cudaStream_t st);
 int simt_chunk(int D);

@@ -329,3 +329,100 @@ def state_combine(T: StateTuple, P: StateTuple, decay: Decay, length: int) -> St
                               _stream(dev))
     _lib.check("pma_state_combine", rc)
     return P
+
+
+# ---------------------------------------------------------------- gated delta-rule variant
+def _gate(t, shape, dev, name):
+    if t is None:
+        return None
+    if not isinstance(t, torch.Tensor):
+        t = torch.tensor(t, dtype=torch.float32)
+    t = t.to(device=dev, dtype=torch.float32)
+    if tuple(t.shape) != tuple(shape):
+        if t.numel() == int(torch.tensor(shape).prod()):
+            t = t.reshape(shape)
+        else:
+            raise ValueError(f"{name} must have shape {tuple(shape)}; got {tuple(t.shape)}")
+    return t.contiguous()
+
+
+def delta_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
+                  alpha: Optional[torch.Tensor], decay: Decay, chunk: int = 64, lyapunov_bound: float = 25.0,
+                  norm_eps: float = 1e-5, state: Optional[torch.Tensor] = None, return_state: bool = True,
+                  out_dtype: Optional[torch.dtype] = None, y_out: Optional[torch.Tensor] = None,
+                  want_y: bool = True):
+    """Gated delta-rule chunked prefill (ChunkedGatedDeltaPrimeAttention's L > 1 core).
+
+    q (pre-scaled), k, v [B,H,L,D]; beta, alpha [B,H,L] float (alpha None: the decay);
+    decay: the module's decay (scalar, [H] or [B,H]) -- the padded tokens of a ragged last
+    chunk decay by it, as in the reference; state [B,H,D,2D] float32 or None.
+    Returns (y [B,H,L,D] or None, final state [B,H,D,2D] or None)."""
+    dev = _require_cuda(q, k, v)
+    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must share one [B,H,L,D] shape")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k, v must share one dtype")
+    B, H, L, D = q.shape
+    L_ = _lib.load()
+    qs, q = _seq(q)
+    ks, k = _seq(k)
+    vs, v = _seq(v)
+    beta = _gate(beta, (B, H, L), dev, "beta")
+    alpha = _gate(alpha, (B, H, L), dev, "alpha")
+    lam, lam_sb = lambda_tensor(decay, B, H, dev)
+    st_in = None
+    if state is not None:
+        st_in = state.to(device=dev, dtype=torch.float32).reshape(B, H, D, 2 * D).contiguous()
+    st_out = torch.empty(B, H, D, 2 * D, device=dev) if return_state else None
+    y = ys = None
+    if want_y:
+        if y_out is not None:
+            if tuple(y_out.shape) != (B, H, L, D) or not _seq_ok(y_out):
+                raise ValueError("y_out must be a [B,H,L,D] tensor with a contiguous, 16-byte aligned last axis")
+            y = y_out
+        else:
+            y = torch.empty(B, H, L, D, dtype=out_dtype or q.dtype, device=dev)
+        ys = ctypes.byref(_seq(y)[0])
+    rc = L_.pma_delta_prefill(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), beta.data_ptr(),
+                              alpha.data_ptr() if alpha is not None else None, lam.data_ptr(), lam_sb, int(chunk),
+                              float(lyapunov_bound), float(norm_eps),
+                              st_in.data_ptr() if st_in is not None else None,
+                              st_out.data_ptr() if st_out is not None else None, ys, _stream(dev))
+    _lib.check("pma_delta_prefill", rc)
+    return y, st_out
+
+
+def delta_decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.Tensor, alpha: torch.Tensor,
+                      state: torch.Tensor, lyapunov_bound: float = 25.0, norm_eps: float = 1e-5,
+                      inplace: bool = False, out_dtype: Optional[torch.dtype] = None,
+                      y_out: Optional[torch.Tensor] = None):
+    """Gated delta-rule L == 1 step: q, k, v [N,H,D]; beta, alpha [N,H]; state [N,H,D,2D].
+    Returns (y [N,H,D], new state); inplace=True updates `state` (contiguous float32)."""
+    dev = _require_cuda(q, k, v)
+    if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must share one [N,H,D] shape")
+    N, H, D = q.shape
+    L_ = _lib.load()
+    qs, q = _seq(q, False)
+    ks, k = _seq(k, False)
+    vs, v = _seq(v, False)
+    beta = _gate(beta, (N, H), dev, "beta")
+    alpha = _gate(alpha, (N, H), dev, "alpha")
+    if tuple(state.shape) != (N, H, D, 2 * D):
+        raise ValueError(f"state must be [N,H,D,2D] = {(N, H, D, 2 * D)}; got {tuple(state.shape)}")
+    if inplace:
+        if state.dtype != torch.float32 or not state.is_contiguous() or state.device != dev:
+            raise ValueError("inplace=True needs a contiguous float32 state on the inputs' device")
+        st_in = st_out = state
+    else:
+        st_in = state.to(device=dev, dtype=torch.float32).contiguous()
+        st_out = torch.empty_like(st_in)
+    y = y_out if y_out is not None else torch.empty(N, H, D, dtype=out_dtype or q.dtype, device=dev)
+    ys, y2 = _seq(y, False)
+    if y2 is not y:
+        raise ValueError("y_out must have a contiguous, 16-byte aligned last axis")
+    rc = L_.pma_delta_decode_step(N, H, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), beta.data_ptr(),
+                                  alpha.data_ptr(), float(lyapunov_bound), float(norm_eps), st_in.data_ptr(),
+                                  st_out.data_ptr(), ctypes.byref(ys), _stream(dev))
+    _lib.check("pma_delta_decode_step", rc)
+    return y, st_out
