@@ -5,11 +5,14 @@
 which keeps the reference's projection / QK-norm / scale code and sends all three
 L branches to libpma.so.  The state tuple format is unchanged, so
 PrimeMomentCache and PrimeForCausalLM (model.py:101-120, 203-242) work as they are.
+`install(ChunkedGatedDeltaPrimeAttention)` does the same for the reference's gated
+delta-rule module (chunked_delta_prime.py:89-283) with delta.delta_forward.
 `uninstall()` restores the original forward.
 """
 from __future__ import annotations
 
 from .attention import moment_forward
+from .delta import delta_forward
 
 _saved: dict = {}
 
@@ -19,14 +22,22 @@ def _default_cls():
     return PrimeMomentAttention
 
 
+def _forward_for(cls):
+    """The kernel forward for a reference class: the gated delta-rule module
+    (chunked_delta_prime.py) has its own state format and core; everything else is the
+    moment-attention forward."""
+    return delta_forward if hasattr(cls, "_build_features") or "Delta" in cls.__name__ else moment_forward
+
+
 def install(cls=None):
-    """Patch `cls.forward` (default: the reference PrimeMomentAttention).  Idempotent."""
+    """Patch `cls.forward` (default: the reference PrimeMomentAttention; also accepts the
+    reference ChunkedGatedDeltaPrimeAttention).  Idempotent."""
     from . import _lib
     _lib.load()  # fail now, not at the first forward, if the library is missing
     cls = cls or _default_cls()
     if cls not in _saved:
         _saved[cls] = cls.__dict__["forward"]
-        cls.forward = moment_forward
+        cls.forward = _forward_for(cls)
     return cls
 
 

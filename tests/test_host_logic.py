@@ -130,3 +130,34 @@ def test_module_dtype_cast_keeps_per_head_decay_float32():
     assert m.decay_per_head.dtype == torch.float32
     assert m.decay_per_head.tolist() == torch.tensor([0.9995, 0.999]).tolist()
     assert m.half().decay_per_head.dtype == torch.float32
+
+
+class DeltaStandIn(nn.Module):
+    """Named like the reference's gated delta-rule module (chunked_delta_prime.py:25)."""
+
+    def _build_features(self, q, k):
+        return q, k
+
+    def forward(self, hidden_states, state=None, return_state=False):
+        return "original", None
+
+
+def test_install_picks_the_delta_forward_for_the_delta_module():
+    pma.install(DeltaStandIn)
+    try:
+        assert DeltaStandIn.forward is pma.delta_forward
+    finally:
+        pma.uninstall(DeltaStandIn)
+    assert DeltaStandIn()(torch.zeros(1, 1, 4))[0] == "original"
+
+
+def test_delta_module_parameters_match_reference_layout():
+    """Parameter names and shapes of chunked_delta_prime.py:53-65, gate biases of :67-71."""
+    m = pma.ChunkedGatedDeltaPrimeAttention(hidden_size=96, num_heads=4, head_dim=16, num_kv_heads=2)
+    shapes = {n: tuple(p.shape) for n, p in m.named_parameters()}
+    assert shapes == {"q_proj.weight": (64, 96), "k_proj.weight": (32, 96), "v_proj.weight": (32, 96),
+                      "o_proj.weight": (96, 64), "erase_proj.weight": (64, 96), "erase_proj.bias": (64,),
+                      "write_proj.weight": (64, 96), "write_proj.bias": (64,), "q_norm.weight": (16,),
+                      "q_norm.bias": (16,), "k_norm.weight": (16,), "k_norm.bias": (16,)}
+    assert torch.all(m.erase_proj.bias == -2.5) and torch.all(m.write_proj.bias == -1.0)
+    assert (m.chunk_size, m.decay, m.lyapunov_bound, m.eps, m.num_kv_groups) == (64, 0.9995, 25.0, 1e-5, 2)
