@@ -8,7 +8,9 @@ tokens/s over all GPUs -- B=8 sequences per GPU, H=12 heads, D=64, L=8192, bf16
 q/k/v, fp32 state, per-head lambda log-uniform in [0.99, 0.9999].  A "step" is one
 pma_prefill call over that batch (y and the final state).  The line also carries
 the config-3 decode step (256 sequences x 12 layers x 12 heads, D=64, one launch
-for all layers' heads, 1000 timed steps) under "decode".
+for all layers' heads, 1000 timed steps) under "decode", and the gated delta-rule variant
+(config-2 prefill with the write gate beta, and its decode step at the config-3 shape) under
+"delta".
 
 Multi-GPU: one process per GPU (torchrun); each rank prefills its own batch x head
 shard with no collective (weak scaling); times are the max over ranks.
@@ -43,6 +45,14 @@ DECODE_BYTES_PER_HEADSTEP = 2 * (2 * 64 * 64 + 3 * 64 + 1) * 4 + 3 * 64 * 2 + 64
 # each kernel on the bench workload; the commands and the rest of the numbers are in profiles/.
 PREFILL_TRAFFIC = 305_104_896 + 78_318_848    # prefill_tc_kernel<0, bf16>, config 2
 DECODE_TRAFFIC = 1_250_602_000 + 1_183_497_000  # decode_step_kernel<64, bf16, bf16>, config 3
+# Gated delta-rule variant (config 2 with the write gate beta): per token-head of the chunked
+# form at C = 64, F = 2D = 128 features -- Gram Phi Phi^T 2*C*F, intra scores Psi Phi^T 2*C*F,
+# inter error Phi S^T 2*F*D, inter readout Psi S^T 2*F*D, state update 2*F*D, intra readout
+# P (beta E) 2*C*D, triangular solve C*D  = 94,208 FLOP; q,k,v in + y out bf16 + beta fp32.
+DELTA_FLOP_PER_TOKHEAD = 4 * 64 * 128 + 6 * 128 * 64 + 3 * 64 * 64
+DELTA_BYTES_PER_TOKHEAD = 8 * 64 + 4
+DELTA_DECODE_BYTES_PER_HEADSTEP = 2 * (64 * 128 * 4) + 4 * 64 * 2 + 8  # state rw + q,k,v,y + beta,alpha
+FP32_SIMT_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal: 148 SMs x 128 FMA/clk at 1,965 MHz
 WORKLOAD = ("config2 prefill: B=8 seqs/GPU, H=12, D=64, L=8192, bf16 q/k/v (QK-normed), fp32 state, "
             "per-head lambda log-U[0.99,0.9999]; step = one pma_prefill (y + final state)")
 
@@ -332,6 +342,103 @@ def bench_decode(args, ws, rank, device, stream, peaks):
             "gpu_launches": dsteps, "clocks": dclk_r}
 
 
+def cpu_delta_sample(target_s: float = 8.0):
+    """The float64 delta-rule port (oracle/pma_oracle.c, single thread) on a bounded sample:
+    one head of config 2 for as many tokens as fit ~target_s seconds."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    from prime_moment_attention_b200 import synth
+    q, k, v = synth.make_qkv(1, 1, 512, 64, seed=7)
+    beta = torch.sigmoid(torch.randn(1, 1, 512, generator=torch.Generator().manual_seed(7)))
+    t0 = time.perf_counter()
+    O.delta_prefill(q, k, v, beta, None, np.array([0.999]))
+    cal = time.perf_counter() - t0
+    L = int(min(8192, max(512, 512 * target_s / max(cal, 1e-6))))
+    q, k, v = synth.make_qkv(1, 1, L, 64, seed=8)
+    beta = torch.sigmoid(torch.randn(1, 1, L, generator=torch.Generator().manual_seed(8)))
+    t0 = time.perf_counter()
+    O.delta_prefill(q, k, v, beta, None, np.array([0.999]))
+    dt = time.perf_counter() - t0
+    return {"value": round(L / dt, 1), "unit": "tok/s per head", "cores": 1, "kind": "port",
+            "sample": f"float64 port of the chunked delta rule (token recurrence), 1 head x L={L}, D=64",
+            "per_token_all_heads_tok_s": round(L / dt / 12, 1)}
+
+
+def bench_delta(args, ws, rank, device, stream, peaks):
+    """Gated delta-rule variant: config-2 prefill with the write gate beta_t = sigmoid(N(0,1)) and
+    retention alpha_t = lambda_h (erase gate off), and the decode step at the config-3 shape."""
+    import torch
+    from prime_moment_attention_b200 import ops, synth
+    hbm_peak, _, peak_kind = peaks
+    c = PREFILL
+    B, H, L, D = args.prefill_batch or c["B"], c["H"], c["L"], c["D"]
+    q, k, v = synth.make_qkv(B, H, L, D, seed=c["seed"] + 1000 * rank, dtype=torch.bfloat16, device=device)
+    lam = synth.make_lambdas(H, *c["lam"], seed=c["seed"]).to(device)
+    g = torch.Generator(device=device).manual_seed(c["seed"] + 17 + rank)
+    beta = torch.sigmoid(torch.randn(B, H, L, device=device, generator=g))
+    y = torch.empty_like(q)
+    st = torch.empty(B, H, D, 2 * D, device=device)
+
+    def step():
+        ops.delta_prefill(q, k, v, beta, None, lam, chunk=64, lyapunov_bound=25.0, y_out=y, return_state=True)
+
+    steps = max(3, min(args.steps, 10))
+    clk = ClockSampler(device.index)
+    clk.start()
+    ms = max_over_ranks(time_steps(step, steps, args.warmup, ws, device, stream), ws, device)
+    clk_r = clk.stop()
+    tokheads = B * L * H
+    tf = tokheads * DELTA_FLOP_PER_TOKHEAD / (ms * 1e-3) / 1e12
+    bw = tokheads * DELTA_BYTES_PER_TOKHEAD / (ms * 1e-3) / 1e9
+    pre = {"metric": "delta_prefill_tok_per_s", "value": round(B * L * ws / (ms * 1e-3), 1), "unit": "tok/s",
+           "ms_per_step": round(ms, 4), "steps": steps, "higher_is_better": True, "dtype": "bf16 in, fp32 math",
+           "config": {"workload": "config2 delta-rule prefill: B=8 seqs/GPU, H=12, D=64, L=8192, chunk 64, bf16 "
+                                  "q/k/v, beta_t=sigmoid(N(0,1)), alpha_t=lambda_h, Lyapunov bound 25"},
+           "roofline": {"bound": "fp32 CUDA cores", "achieved": round(tf, 2), "peak": round(FP32_SIMT_PEAK_TFLOPS, 1),
+                        "unit": "TFLOP/s", "frac": round(tf / FP32_SIMT_PEAK_TFLOPS, 4), "traffic": None,
+                        "peak_kind": "nominal (148 SMs x 128 FMA/clk x 1965 MHz); one CTA per head-state, "
+                                     f"{min(B * H, 148)} of 148 SMs busy",
+                        "hbm": {"achieved": round(bw, 1), "peak": hbm_peak, "unit": "GB/s",
+                                "frac": round(bw / hbm_peak, 4), "peak_kind": peak_kind},
+                        "algorithmic_flop_per_launch": tokheads * DELTA_FLOP_PER_TOKHEAD},
+           "gpu_launches": steps, "clocks": clk_r}
+    del q, k, v, y, beta, st
+    torch.cuda.empty_cache()
+
+    dc = DECODE
+    N, HD = dc["seqs"], dc["layers"] * dc["H"]
+    lam_d = synth.make_lambdas(HD, *dc["lam"], seed=dc["seed"]).to(device)
+    S = torch.randn(N, HD, D, 2 * D, device=device, generator=g) * dc["sigma"]
+    toks = [synth.make_decode_tokens(N, HD, D, seed=dc["seed"] * 100 + i, device=device) for i in range(8)]
+    bd = torch.sigmoid(torch.randn(N, HD, device=device, generator=g))
+    ad = lam_d.view(1, HD).expand(N, HD).contiguous()
+    yd = torch.empty(N, HD, D, dtype=torch.bfloat16, device=device)
+    it = [0]
+
+    def dstep():
+        qq, kk, vv = toks[it[0] & 7]
+        it[0] += 1
+        ops.delta_decode_step(qq, kk, vv, bd, ad, S, lyapunov_bound=25.0, inplace=True, y_out=yd)
+
+    dsteps = min(args.decode_steps or 200, 200)
+    dclk = ClockSampler(device.index)
+    dclk.start()
+    dms = max_over_ranks(time_steps(dstep, dsteps, max(3, args.warmup), ws, device, stream), ws, device)
+    dclk_r = dclk.stop()
+    d_bytes = N * HD * DELTA_DECODE_BYTES_PER_HEADSTEP
+    d_bw = d_bytes / (dms * 1e-3) / 1e9
+    dec = {"metric": "delta_decode_step_us", "value": round(dms * 1e3, 2), "unit": "us/step",
+           "higher_is_better": False, "steps": dsteps,
+           "config": {"workload": "config3-shape delta decode: 256 seqs x 12 layers x 12 heads per GPU, D=64, "
+                                  "state [D,2D] fp32 in place (1.21 GB), bf16 q/k/v, one launch"},
+           "roofline": {"bound": "hbm", "achieved": round(d_bw, 1), "peak": hbm_peak, "unit": "GB/s",
+                        "frac": round(d_bw / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+                        "algorithmic_bytes_per_launch": d_bytes},
+           "gpu_launches": dsteps, "clocks": dclk_r}
+    return {"prefill": pre, "decode": dec}
+
+
 def run_ours(args):
     import torch
     ws, rank, local = dist_setup()
@@ -350,6 +457,15 @@ def run_ours(args):
         else:
             line = dict(dec, n_gpus=ws, warmup=args.warmup, scaling="weak", dtype="bf16", data="synthetic",
                         vs_baseline=None)
+        torch.cuda.empty_cache()
+    if args.workload in ("both", "delta"):
+        dl = bench_delta(args, ws, rank, device, stream, peaks)
+        if line:
+            line["delta"] = dl
+        else:
+            line = dict(dl["prefill"], n_gpus=ws, warmup=args.warmup, scaling="weak", data="synthetic",
+                        vs_baseline=None, delta_decode=dl["decode"])
+        torch.cuda.empty_cache()
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and ref_bench_path():
         try:
             if "decode" in line:
@@ -358,6 +474,11 @@ def run_ours(args):
                 line["cpu_baseline"] = cpu_prefill_sample()
         except Exception as e:  # the baseline must not sink the GPU number
             line["cpu_baseline"] = {"error": str(e)[:200]}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and "delta" in line:
+        try:
+            line["delta"]["prefill"]["cpu_baseline"] = cpu_delta_sample()
+        except Exception as e:
+            line["delta"]["prefill"]["cpu_baseline"] = {"error": str(e)[:200]}
     if rank == 0:
         print(json.dumps(line))
     if ws > 1:
@@ -373,8 +494,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["both", "prefill", "decode"], default="both",
-                    help="profiling aid: run only one part (the JSON line then lacks the other)")
+    ap.add_argument("--workload", choices=["both", "prefill", "decode", "delta"], default="both",
+                    help="profiling aid: run only one part (the JSON line then lacks the others)")
     ap.add_argument("--prefill-batch", type=int, default=0,
                     help="profiling aid: sequences per GPU for the prefill part (default: config 2's 8)")
     ap.add_argument("--decode-steps", type=int, default=0,
