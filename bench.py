@@ -10,7 +10,7 @@ pma_prefill call over that batch (y and the final state).  The line also carries
 the config-3 decode step (256 sequences x 12 layers x 12 heads, D=64, one launch
 for all layers' heads, 1000 timed steps) under "decode", and the gated delta-rule variant
 (config-2 prefill with the write gate beta, and its decode step at the config-3 shape) under
-"delta".
+"delta", and the config-4 model (prefill and CUDA-graph decode) under "model".
 
 Multi-GPU: one process per GPU (torchrun); each rank prefills its own batch x head
 shard with no collective (weak scaling); times are the max over ranks.
@@ -439,6 +439,60 @@ def bench_delta(args, ws, rank, device, stream, peaks):
     return {"prefill": pre, "decode": dec}
 
 
+MODEL = dict(vocab=50257, hidden=768, layers=12, heads=12, head_dim=64, mlp=3072, decay=0.9995, batch=64, L=4096,
+             new_tokens=256, seed=4)
+
+
+def bench_model(args, ws, rank, device, stream, peaks):
+    """Config 4: PRIME-125M shape (random-init bf16, SwiGLU MLP 3072, tied embeddings, QK-norm) on
+    this package's PrimeForCausalLM.  Prefill of 64 sequences x 4096 uniform token ids (split over
+    the ranks: data-parallel by sequence, strong scaling), then greedy decode steps from the
+    prefilled states with the whole step in one CUDA graph."""
+    import torch
+    from prime_moment_attention_b200.model import DecodeGraph, PrimeConfig, PrimeForCausalLM
+    _, tc_peak, peak_kind = peaks
+    c = MODEL
+    cfg = PrimeConfig(vocab_size=c["vocab"], hidden_size=c["hidden"], num_layers=c["layers"], num_heads=c["heads"],
+                      head_dim=c["head_dim"], intermediate_size=c["mlp"], decay=c["decay"], use_qk_norm=True)
+    torch.manual_seed(c["seed"])
+    m = PrimeForCausalLM(cfg).to(device, torch.bfloat16).eval()
+    B = max(1, c["batch"] // ws)
+    g = torch.Generator(device=device).manual_seed(c["seed"] + rank)
+    ids = torch.randint(0, c["vocab"], (B, c["L"]), device=device, generator=g)
+    with torch.inference_mode():
+        def pstep():
+            return m(ids, return_states=True, last_logits_only=True)
+
+        clk = ClockSampler(device.index)
+        clk.start()
+        ms = max_over_ranks(time_steps(pstep, 3, 3, ws, device, stream), ws, device)
+        clk_r = clk.stop()
+        out = pstep()
+        first = torch.argmax(out["logits"][:, -1], dim=-1, keepdim=True)
+        dg = DecodeGraph(m, out["states"], first)
+        del out
+        dms = max_over_ranks(time_steps(dg.step, c["new_tokens"], 3, ws, device, stream), ws, device)
+    # per token: 2 x the layer weights (the tied embedding / head is excluded: the head runs on the
+    # last position only) + the moment core's chunked work per head and layer
+    n_params = sum(p.numel() for n, p in m.named_parameters() if "embed" not in n)
+    flop_tok = 2 * n_params + c["layers"] * c["heads"] * PREFILL_FLOP_PER_TOKHEAD
+    tf = B * c["L"] * flop_tok / (ms * 1e-3) / 1e12
+    return {"metric": "model_prefill_tok_per_s", "value": round(B * c["L"] * ws / (ms * 1e-3), 1), "unit": "tok/s",
+            "ms_per_step": round(ms, 3), "steps": 3, "higher_is_better": True, "scaling": "strong",
+            "dtype": "bf16",
+            "config": {"workload": "config4 PRIME-125M shape, random init bf16: 12 layers, d 768, 12x64 heads, "
+                                   "SwiGLU 3072 (the reference MLP; BASELINE says GELU), vocab 50257 tied, QK-norm; "
+                                   f"{c['batch']} seqs x {c['L']} uniform ids over {ws} GPU(s), last-position logits",
+                       "batch_per_gpu": B},
+            "decode": {"metric": "model_decode_step_us", "value": round(dms * 1e3, 1), "unit": "us/step",
+                       "tok_per_s": round(B * ws / (dms * 1e-3), 1), "steps": c["new_tokens"],
+                       "path": "whole greedy step (embed, 12 layers, head, argmax) in one CUDA graph, states in place"},
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                         "frac": round(tf / tc_peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "flop_per_token": flop_tok},
+            "gpu_launches": None, "clocks": clk_r}
+
+
 def run_ours(args):
     import torch
     ws, rank, local = dist_setup()
@@ -457,6 +511,13 @@ def run_ours(args):
         else:
             line = dict(dec, n_gpus=ws, warmup=args.warmup, scaling="weak", dtype="bf16", data="synthetic",
                         vs_baseline=None)
+        torch.cuda.empty_cache()
+    if args.workload in ("both", "model"):
+        md = bench_model(args, ws, rank, device, stream, peaks)
+        if line:
+            line["model"] = md
+        else:
+            line = dict(md, n_gpus=ws, warmup=args.warmup, data="synthetic", vs_baseline=None)
         torch.cuda.empty_cache()
     if args.workload in ("both", "delta"):
         dl = bench_delta(args, ws, rank, device, stream, peaks)
@@ -494,7 +555,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["both", "prefill", "decode", "delta"], default="both",
+    ap.add_argument("--workload", choices=["both", "prefill", "decode", "delta", "model"], default="both",
                     help="profiling aid: run only one part (the JSON line then lacks the others)")
     ap.add_argument("--prefill-batch", type=int, default=0,
                     help="profiling aid: sequences per GPU for the prefill part (default: config 2's 8)")
