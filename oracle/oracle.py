@@ -46,6 +46,8 @@ def lib() -> ctypes.CDLL:
         L.orc_delta_prefill.restype = ctypes.c_int
         L.orc_delta_step.argtypes = [ctypes.c_int] * 3 + [_dp] * 5 + [ctypes.c_double] * 2 + [_dp] * 3
         L.orc_delta_step.restype = ctypes.c_int
+        L.orc_selective_prefill.argtypes = [ctypes.c_int] * 4 + [_dp] * 5 + [ctypes.c_double] + [_dp] * 7
+        L.orc_selective_prefill.restype = ctypes.c_int
         _LIB = L
     return _LIB
 
@@ -168,3 +170,21 @@ def delta_step(q, k, v, beta, alpha, state, bound: float = 25.0, norm_eps: float
     if rc != 0:
         raise ValueError("orc_delta_step rejected its arguments")
     return y, st
+
+
+def selective_prefill(q, k, v, log_decay, beta, state=None, eps: float = 1.0):
+    """Selective moment attention (selective.py:264-444) as its step recurrence: q (pre-scaled),
+    k, v [B,H,L,D]; log_decay [B,H,L] = -Delta_t / tau_h; beta [H]; state in the reference's
+    selective layout (S2, K2 carry the 1/2 beta^2 factor).  Returns (y, state)."""
+    q, k, v = _f64(q), _f64(k), _f64(v)
+    B, H, L, D = q.shape
+    ld = np.ascontiguousarray(_f64(log_decay).reshape(B, H, L))
+    bt = np.ascontiguousarray(_f64(beta).reshape(H))
+    st = [np.array(_f64(s), copy=True) for s in (state if state is not None else zero_state(B, H, D))]
+    st[3] = st[3].reshape(B, H, 1)
+    y = np.zeros_like(q)
+    rc = lib().orc_selective_prefill(B, H, L, D, _ptr(q), _ptr(k), _ptr(v), _ptr(ld), _ptr(bt), float(eps),
+                                     *[_ptr(s) for s in st], _ptr(y))
+    if rc != 0:
+        raise ValueError("orc_selective_prefill rejected its arguments")
+    return y, tuple(st)

@@ -31,8 +31,9 @@
  *                     chunked core mishandles (chunked_ssd.py:129-137 broadcasts
  *                     [B,H,1,D] against [1,1,nc,1,1]).
  *
- *   orc_delta_prefill / orc_delta_step   the gated delta-rule variant (see the
- *                     section at the end of this file).
+ *   orc_delta_prefill / orc_delta_step   the gated delta-rule variant, and
+ *   orc_selective_prefill                the selective variant (see the sections at
+ *                     the end of this file).
  *
  * Extension over the reference: lambda may differ per head (and per batch row).
  * The reference holds one scalar decay per module (attention.py:49); heads are
@@ -282,5 +283,58 @@ int orc_delta_step(int N, int H, int D, const double *q, const double *k, const 
         delta_lyapunov((int)SZ, bound, S);
         if (y) delta_readout(D, S, psi, y + i * D);
     }
+    return ORC_OK;
+}
+
+/* ---------------------------------------------------------------------------
+ * Selective variant: PrimeSelectiveMomentAttention
+ * (src/prime_moment_attention/selective.py:264-444).  Per token a decay
+ * lambda_t = exp(-Delta_t / tau_h), given here as log_decay[t] = -Delta_t / tau_h, and a
+ * per-head temperature beta_h.  The step branch (:367-396), iterated:
+ *     S0 = l S0 + v             Z0 = l Z0 + 1
+ *     S1 = l S1 + b k v^T       Z1 = l Z1 + b k
+ *     S2 = l S2 + b^2/2 k^2 v^T Z2 = l Z2 + b^2/2 k^2
+ *     y  = (S0 + q.S1 + q^2.S2) / max(Z0 + q.Z1 + q^2.Z2, eps)
+ * (no 1/2 at the readout: the reference folds it into S2 / Z2, which therefore hold half of
+ * the moment-attention layout's second moments).  Its parallel branch (:401-435) is the same
+ * recurrence from a zero state.
+ *   q,k,v,y [B,H,L,D]; log_decay [B,H,L]; beta [H]; state arrays as orc_prefill.
+ * ------------------------------------------------------------------------- */
+int orc_selective_prefill(int B, int H, int L, int D, const double *q, const double *k, const double *v,
+                          const double *log_decay, const double *beta, double eps,
+                          double *S0, double *S1, double *S2, double *Z0, double *Z1, double *Z2, double *y)
+{
+    if (B < 0 || H <= 0 || L < 0 || D <= 0 || !log_decay || !beta) return ORC_EINVAL;
+    for (int b = 0; b < B; ++b)
+        for (int h = 0; h < H; ++h) {
+            const size_t i = (size_t)b * H + h;
+            const double bt = beta[h], b2 = 0.5 * bt * bt;
+            double *s0 = S0 + i * D, *s1 = S1 + i * D * D, *s2 = S2 + i * D * D;
+            double *z1 = Z1 + i * D, *z2 = Z2 + i * D;
+            for (int t = 0; t < L; ++t) {
+                const size_t o = (i * (size_t)L + t) * D;
+                const double l = exp(log_decay[i * (size_t)L + t]);
+                const double *qt = q + o, *kt = k + o, *vt = v + o;
+                for (int e = 0; e < D; ++e) s0[e] = l * s0[e] + vt[e];
+                for (int d = 0; d < D; ++d)
+                    for (int e = 0; e < D; ++e) {
+                        s1[d * D + e] = l * s1[d * D + e] + bt * kt[d] * vt[e];
+                        s2[d * D + e] = l * s2[d * D + e] + b2 * kt[d] * kt[d] * vt[e];
+                    }
+                Z0[i] = l * Z0[i] + 1.0;
+                double den = Z0[i];
+                for (int d = 0; d < D; ++d) {
+                    z1[d] = l * z1[d] + bt * kt[d];
+                    z2[d] = l * z2[d] + b2 * kt[d] * kt[d];
+                    den += qt[d] * z1[d] + qt[d] * qt[d] * z2[d];
+                }
+                if (den < eps) den = eps;
+                for (int e = 0; e < D; ++e) {
+                    double num = s0[e];
+                    for (int d = 0; d < D; ++d) num += qt[d] * s1[d * D + e] + qt[d] * qt[d] * s2[d * D + e];
+                    y[o + e] = num / den;
+                }
+            }
+        }
     return ORC_OK;
 }
