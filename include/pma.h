@@ -328,6 +328,41 @@ PMA_API int pma_delta_decode_step(int N, int H, int D,
                                   const pma_seq_tensor *y, pma_stream_t stream);
 
 /*
+ * Selective variant (PrimeSelectiveMomentAttention, src/prime_moment_attention/selective.py:264-444):
+ * the moment recurrence with a decay per token, lambda_t = exp(-Delta_t / tau_h), and a
+ * temperature beta_h per head on k:
+ *     S0 = l S0 + v,  S1 = l S1 + b k v^T,  S2 = l S2 + b^2/2 k^2 v^T,  Z0 = l Z0 + 1,
+ *     Z1 = l Z1 + b k,  Z2 = l Z2 + b^2/2 k^2,
+ *     y = (S0 + q.S1 + q^2.S2) / max(Z0 + q.Z1 + q^2.Z2, eps)
+ * States use the reference's selective layout (the 1/2 b^2 sits in S2 and Z2).
+ *
+ * Prefill over L tokens (the reference's parallel branch, :401-435, and its step branch iterated
+ * when a state is given -- the reference's parallel branch ignores an incoming state; this entry
+ * carries it, as the step branch does).
+ *   log_decay   device float [B,H,L] contiguous: -Delta_t / tau_h.
+ *   beta        device float [H]: the temperature (clamp(exp(log_beta), 0.1, 15) in the module).
+ *   prologue    as pma_prefill_ex (GQA map, QK-norm, q scale) or NULL.
+ * Computed in float32 on CUDA cores for every D in {16, 32, 64, 128} and both input dtypes.
+ */
+PMA_API int pma_selective_prefill(int B, int H, int L, int D,
+                                  const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                                  const pma_prologue *prologue, const float *log_decay, const float *beta,
+                                  const pma_state *state_in, const pma_state *state_out,
+                                  float eps, const pma_seq_tensor *y, pma_stream_t stream);
+
+/*
+ * Selective decode step (the L == 1 branch, selective.py:367-396): log_decay [N,H]
+ * (-Delta_t / tau_h of this token), beta [H]; rows / pool_rows as pma_decode_step_ex
+ * (NULL rows: state row n).  state_in and state_out may be the same arrays.
+ */
+PMA_API int pma_selective_decode_step(int N, int H, int D,
+                                      const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                                      const pma_prologue *prologue, const float *log_decay, const float *beta,
+                                      const int32_t *rows, int pool_rows,
+                                      const pma_state *state_in, const pma_state *state_out,
+                                      float eps, const pma_seq_tensor *y, pma_stream_t stream);
+
+/*
  * Segment carry: P <- lambda^len * P + T for B x H head-states, elementwise over
  * all six components.  len = tokens in the segment that produced T.
  * This is the associative step of the reference's inter-chunk scan

@@ -6,6 +6,7 @@ of include/pma.h (libpma.so), with a host-side mirror of the reference interface
 
     PrimeMomentAttention, chunked_prime_ssd_core, PrimeMomentCache   (same API as the reference)
     ChunkedGatedDeltaPrimeAttention                                   (gated delta-rule variant)
+    PrimeSelectiveMomentAttention                                     (selective variant)
     install(), uninstall()                                            (patch the reference module)
     ops.prefill, ops.decode_step, ops.state_combine                   (torch-facing C-ABI calls)
     sp.sequence_parallel_prefill                                      (sequence shards over GPUs)
@@ -13,9 +14,11 @@ of include/pma.h (libpma.so), with a host-side mirror of the reference interface
 from .attention import PrimeMomentAttention, chunked_prime_ssd_core, moment_forward
 from .cache import PrimeMomentCache
 from .delta import ChunkedGatedDeltaPrimeAttention, delta_forward
+from .selective import PrimeSelectiveMomentAttention, selective_forward
 from .shim import install, installed, uninstall
 from . import ops
 
 __all__ = ["PrimeMomentAttention", "chunked_prime_ssd_core", "moment_forward", "PrimeMomentCache",
-           "ChunkedGatedDeltaPrimeAttention", "delta_forward", "install",
+           "ChunkedGatedDeltaPrimeAttention", "delta_forward", "PrimeSelectiveMomentAttention",
+           "selective_forward", "install",
            "uninstall", "installed", "ops"]

@@ -109,6 +109,14 @@ def load() -> ctypes.CDLL:
                                         + [ctypes.c_float] * 2 + [ctypes.c_void_p] * 2
                                         + [_P(SeqTensor), ctypes.c_void_p])
     L.pma_delta_decode_step.restype = ctypes.c_int
+    L.pma_selective_prefill.argtypes = ([ctypes.c_int] * 4 + [_P(SeqTensor)] * 3 + [_P(Prologue)]
+                                        + [ctypes.c_void_p] * 2 + [_P(State)] * 2
+                                        + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p])
+    L.pma_selective_prefill.restype = ctypes.c_int
+    L.pma_selective_decode_step.argtypes = ([ctypes.c_int] * 3 + [_P(SeqTensor)] * 3 + [_P(Prologue)]
+                                            + [ctypes.c_void_p] * 2 + [ctypes.c_void_p, ctypes.c_int]
+                                            + [_P(State)] * 2 + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p])
+    L.pma_selective_decode_step.restype = ctypes.c_int
     L.pma_state_combine.argtypes = ([ctypes.c_int] * 3 + [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64]
                                     + [_P(State)] * 2 + [ctypes.c_void_p])
     L.pma_state_combine.restype = ctypes.c_int

@@ -44,7 +44,10 @@ __global__ void __launch_bounds__(256) decode_step_kernel(const DecodeParams p) 
         if (srow < 0 || srow >= p.pool_rows) return;
     }
     const int idx = srow * p.H + h;                  // head-state index in the state arrays
-    const float lam = p.lambda[(int64_t)n * p.lam_sn + h];
+    const float lraw = p.lambda[(int64_t)n * p.lam_sn + h];
+    const float lam = p.log_lambda ? expf(lraw) : lraw;
+    // second moments: k^2 v added with c2, read out with cq (moment layout 1, 1/2; selective 1/2, 1)
+    const float c2 = p.half_sq ? 0.5f : 1.0f, cq = p.half_sq ? 1.0f : 0.5f;
 
     const TI *qp = reinterpret_cast<const TI *>(p.q.p) + n * p.q.sb + h * p.q.sh;
     const int hk = h / p.pro.groups;                 // GQA: the kv head this query head reads
@@ -61,9 +64,10 @@ __global__ void __launch_bounds__(256) decode_step_kernel(const DecodeParams p) 
         for (int d = lane; d < D; d += 32)
             sq[warp][d] = prologue_elem(sq[warp][d], st, p.pro.qw, p.pro.qb, d, p.pro.q_scale);
     }
-    if (p.pro.k_work()) {
-        const float2 st = warp_row_stats<D>(sk[warp], p.pro.ln_eps, lane);
-        for (int d = lane; d < D; d += 32) sk[warp][d] = prologue_elem(sk[warp][d], st, p.pro.kw, p.pro.kb, d, 1.f);
+    if (p.pro.k_work() || p.k_head_scale) {
+        const float ks = p.k_head_scale ? p.k_head_scale[h] : 1.f;
+        const float2 st = p.pro.kw ? warp_row_stats<D>(sk[warp], p.pro.ln_eps, lane) : make_float2(0.f, 1.f);
+        for (int d = lane; d < D; d += 32) sk[warp][d] = prologue_elem(sk[warp][d], st, p.pro.kw, p.pro.kb, d, ks);
     }
     __syncwarp();
 
@@ -87,7 +91,7 @@ __global__ void __launch_bounds__(256) decode_step_kernel(const DecodeParams p) 
         for (int j = 0; j < BATCH; ++j) {
             const int d = r0 + RPI * (i0 + j);
             const float kd = sk[warp][d], qd = sq[warp][d];
-            const float kd2 = kd * kd, qh2 = 0.5f * qd * qd;
+            const float kd2 = c2 * kd * kd, qh2 = cq * qd * qd;
             float4 s1 = fma4(lam, a[j], scale4(kd, v4));
             float4 s2 = fma4(lam, b[j], scale4(kd2, v4));
             stcs4(S1o + d * D + c0, s1);
@@ -111,10 +115,10 @@ __global__ void __launch_bounds__(256) decode_step_kernel(const DecodeParams p) 
     for (int d = lane; d < D; d += 32) {
         const float kd = sk[warp][d], qd = sq[warp][d];
         const float z1 = fmaf(lam, p.in.Z1[voff + d], kd);
-        const float z2 = fmaf(lam, p.in.Z2[voff + d], kd * kd);
+        const float z2 = fmaf(lam, p.in.Z2[voff + d], c2 * kd * kd);
         p.out.Z1[voff + d] = z1;
         p.out.Z2[voff + d] = z2;
-        dpart = fmaf(qd, z1, fmaf(0.5f * qd * qd, z2, dpart));
+        dpart = fmaf(qd, z1, fmaf(cq * qd * qd, z2, dpart));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) dpart += __shfl_xor_sync(0xffffffffu, dpart, o);

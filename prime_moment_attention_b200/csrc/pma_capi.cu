@@ -150,7 +150,8 @@ int prefill_impl(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_
 int decode_impl(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
                 const pma_prologue *prologue, const float *lambda, int64_t lambda_stride_n, const int32_t *rows,
                 int pool_rows, const pma_state *state_in, const pma_state *state_out, float eps,
-                const pma_seq_tensor *y, pma_stream_t stream);
+                const pma_seq_tensor *y, pma_stream_t stream, const float *k_head_scale = nullptr,
+                bool selective = false);
 
 bool bf16_exact(float f) {
     uint32_t u;
@@ -401,7 +402,7 @@ int prefill_impl(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_
 int decode_impl(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
                 const pma_prologue *prologue, const float *lambda, int64_t lambda_stride_n, const int32_t *rows,
                 int pool_rows, const pma_state *state_in, const pma_state *state_out, float eps,
-                const pma_seq_tensor *y, pma_stream_t stream) {
+                const pma_seq_tensor *y, pma_stream_t stream, const float *k_head_scale, bool selective) {
     if (N < 0 || H <= 0 || !lambda || lambda_stride_n < 0 || pool_rows < 0) return PMA_ERR_ARGUMENT;
     if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
     int rc;
@@ -432,6 +433,9 @@ int decode_impl(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tens
     p.eps = eps;
     p.rows = rows;
     p.pool_rows = rows ? pool_rows : 0;
+    p.k_head_scale = k_head_scale;
+    p.log_lambda = selective ? 1 : 0;
+    p.half_sq = selective ? 1 : 0;
     cudaError_t e = launch_decode(p, D, q->dtype, y->dtype, reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? PMA_OK : cuda_fail(e);
 }
@@ -522,6 +526,79 @@ int pma_delta_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pm
     p.state_out = state_out;
     cudaError_t e = launch_delta_step(p, D, q->dtype, y->dtype, reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? PMA_OK : cuda_fail(e);
+}
+
+int pma_selective_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                          const pma_seq_tensor *v, const pma_prologue *prologue, const float *log_decay,
+                          const float *beta, const pma_state *state_in, const pma_state *state_out, float eps,
+                          const pma_seq_tensor *y, pma_stream_t stream) {
+    if (B < 0 || H <= 0 || L < 0 || !beta || (L > 0 && B > 0 && !log_decay)) return PMA_ERR_ARGUMENT;
+    if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
+    int rc;
+    Prologue pro;
+    if ((rc = prologue_of(prologue, H, &pro))) return rc;
+    const bool empty = (L == 0 || B == 0);
+    if ((rc = check_seq(q, true, empty)) || (rc = check_seq(k, true, empty)) || (rc = check_seq(v, true, empty)))
+        return rc;
+    if (q->dtype != k->dtype || q->dtype != v->dtype) return PMA_ERR_DTYPE;
+    if (y && (rc = check_seq(y, true, empty))) return rc;
+    if (state_in && (rc = check_state(state_in))) return rc;
+    if (state_out && (rc = check_state(state_out))) return rc;
+    if (!y && !state_out) return PMA_OK;
+    DevInfo di;
+    if ((rc = device_info(&di))) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int BH = B * H;
+    if (BH == 0) return PMA_OK;
+    if (L == 0) {  // the state passes through unchanged (same layout in and out)
+        if (!state_out) return PMA_OK;
+        const size_t DD = (size_t)D * D;
+        float *dst[6] = {state_out->S0, state_out->S1, state_out->S2, state_out->Z0, state_out->Z1, state_out->Z2};
+        const float *src[6] = {state_in ? state_in->S0 : nullptr, state_in ? state_in->S1 : nullptr,
+                               state_in ? state_in->S2 : nullptr, state_in ? state_in->Z0 : nullptr,
+                               state_in ? state_in->Z1 : nullptr, state_in ? state_in->Z2 : nullptr};
+        const size_t n[6] = {BH * (size_t)D, BH * DD, BH * DD, (size_t)BH, BH * (size_t)D, BH * (size_t)D};
+        for (int i = 0; i < 6; ++i) {
+            cudaError_t e = src[i] ? (src[i] == dst[i] ? cudaSuccess
+                                                        : cudaMemcpyAsync(dst[i], src[i], n[i] * 4,
+                                                                          cudaMemcpyDeviceToDevice, st))
+                                   : cudaMemsetAsync(dst[i], 0, n[i] * 4, st);
+            if (e != cudaSuccess) return cuda_fail(e);
+        }
+        return PMA_OK;
+    }
+    PrefillParams p{};
+    p.B = B;
+    p.H = H;
+    p.L = L;
+    p.seg_len = ((L + simt_chunk(D) - 1) / simt_chunk(D)) * simt_chunk(D);
+    p.q = seq_of(q);
+    p.k = seq_of(k);
+    p.v = seq_of(v);
+    p.pro = pro;
+    p.y = seqout_of(y);
+    p.lambda = beta;  // not read on the per-token path; any valid pointer
+    p.lam_sb = 0;
+    p.in = user_ref(state_in);
+    p.out = user_ref(state_out);
+    p.eps = eps;
+    p.state_only = 0;
+    p.status = nullptr;
+    p.logdecay = log_decay;
+    p.k_head_scale = beta;
+    p.half_sq = 1;
+    cudaError_t e = launch_prefill_simt(p, D, q->dtype, y ? y->dtype : PMA_F32, dim3(BH, 1), st);
+    return e == cudaSuccess ? PMA_OK : cuda_fail(e);
+}
+
+int pma_selective_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                              const pma_seq_tensor *v, const pma_prologue *prologue, const float *log_decay,
+                              const float *beta, const int32_t *rows, int pool_rows, const pma_state *state_in,
+                              const pma_state *state_out, float eps, const pma_seq_tensor *y,
+                              pma_stream_t stream) {
+    if (!beta) return PMA_ERR_ARGUMENT;
+    return decode_impl(N, H, D, q, k, v, prologue, log_decay, H, rows, pool_rows, state_in, state_out, eps, y,
+                       stream, beta, true);
 }
 
 int pma_state_combine(int B, int H, int D, const float *lambda, int64_t lambda_stride_b, int64_t len,

@@ -21,6 +21,10 @@ struct PrefillParams {
     float eps;
     int state_only;       // 1: skip the readout, start every segment from zero, write its state to `out`
     int *status;          // device status word (0 = ok); bounded waits record a code here
+    // selective variant (CUDA-core kernel only, one segment):
+    const float *logdecay;      // [B*H*L] log lambda_t per token, or nullptr (lambda per head)
+    const float *k_head_scale;  // [H] k multiplied by it (the temperature beta_h), or nullptr
+    int half_sq;                // 1: user states hold S2, Z2 halved (the selective layout)
 };
 
 // Workspace layout: [header: 256 B, int status word first][per-segment states, float32].
@@ -37,6 +41,9 @@ struct DecodeParams {
     float eps;
     const int32_t *rows;    // nullable: state row of batch row n (a state pool), else n
     int pool_rows;          // rows in the pool (bounds for `rows`)
+    int log_lambda;         // 1: `lambda` holds log lambda (the selective variant's per-token decay)
+    const float *k_head_scale;  // [H] or nullptr: k multiplied by it
+    int half_sq;            // 1: S2, Z2 held halved, read out without the 1/2 (selective layout)
 };
 
 // Gated delta-rule variant (delta.cu).  State per head-state: S [D][2D] float32, row-major.

@@ -10,10 +10,10 @@
 
 namespace pma {
 
-template <int D, int C, typename TI, typename TO>
+template <int D, int C, typename TI, typename TO, bool PT>
 __global__ void __launch_bounds__(256) prefill_simt_kernel(const PrefillParams p) {
     extern __shared__ float4 smem4[];
-    simt_prefill_body<D, C, TI, TO>(p, reinterpret_cast<float *>(smem4), blockIdx.x, blockIdx.y);
+    simt_prefill_body<D, C, TI, TO, PT>(p, reinterpret_cast<float *>(smem4), blockIdx.x, blockIdx.y);
 }
 
 // ---------------------------------------------------------------------------
@@ -86,14 +86,19 @@ __global__ void state_combine_kernel(int BH, int H, int D, const float *lambda, 
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
-template <int D, int C, typename TI, typename TO>
-static cudaError_t launch_simt_t(const PrefillParams &p, dim3 grid, cudaStream_t st) {
+template <int D, int C, typename TI, typename TO, bool PT>
+static cudaError_t launch_simt_pt(const PrefillParams &p, dim3 grid, cudaStream_t st) {
     const size_t smem = SimtSmem<D, C>::bytes;
-    auto kern = prefill_simt_kernel<D, C, TI, TO>;
-    cudaError_t e = set_smem_once<prefill_simt_kernel<D, C, TI, TO>>((int)smem);
+    auto kern = prefill_simt_kernel<D, C, TI, TO, PT>;
+    cudaError_t e = set_smem_once<prefill_simt_kernel<D, C, TI, TO, PT>>((int)smem);
     if (e != cudaSuccess) return e;
     kern<<<grid, 256, smem, st>>>(p);
     return cudaGetLastError();
+}
+
+template <int D, int C, typename TI, typename TO>
+static cudaError_t launch_simt_t(const PrefillParams &p, dim3 grid, cudaStream_t st) {
+    return p.logdecay ? launch_simt_pt<D, C, TI, TO, true>(p, grid, st) : launch_simt_pt<D, C, TI, TO, false>(p, grid, st);
 }
 
 template <int D, int C>

@@ -23,12 +23,12 @@ import torch.nn.functional as F
 
 from . import ops
 from .attention import PrimeMomentAttention, _prologue
+from .selective import PrimeSelectiveMomentAttention
 
 
 @dataclass
 class PrimeConfig:
-    """Same fields and defaults as the reference PrimeConfig (model.py:20-44); the selective
-    variant (use_selective) is not part of this package."""
+    """Same fields and defaults as the reference PrimeConfig (model.py:20-44)."""
     vocab_size: int = 32000
     hidden_size: int = 512
     num_layers: int = 6
@@ -51,8 +51,6 @@ class PrimeConfig:
             self.num_kv_heads = self.num_heads
         if self.intermediate_size is None:
             self.intermediate_size = int(2 * (4 * self.hidden_size) / 3)
-        if self.use_selective:
-            raise NotImplementedError("selective moment attention is not part of this package")
 
 
 class RMSNorm(nn.Module):
@@ -86,9 +84,16 @@ class PrimeBlock(nn.Module):
     def __init__(self, config: PrimeConfig):
         super().__init__()
         self.input_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
-        self.self_attn = PrimeMomentAttention(hidden_size=config.hidden_size, num_heads=config.num_heads,
-                                              head_dim=config.head_dim, num_kv_heads=config.num_kv_heads,
-                                              decay=config.decay, use_qk_norm=config.use_qk_norm, eps=config.eps)
+        if config.use_selective:
+            self.self_attn = PrimeSelectiveMomentAttention(
+                hidden_size=config.hidden_size, num_heads=config.num_heads, head_dim=config.head_dim,
+                num_kv_heads=config.num_kv_heads, decay=config.decay, use_qk_norm=config.use_qk_norm,
+                eps=config.eps, min_tau=config.min_tau, max_tau=config.max_tau)
+        else:
+            self.self_attn = PrimeMomentAttention(hidden_size=config.hidden_size, num_heads=config.num_heads,
+                                                  head_dim=config.head_dim, num_kv_heads=config.num_kv_heads,
+                                                  decay=config.decay, use_qk_norm=config.use_qk_norm,
+                                                  eps=config.eps)
         self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
         self.mlp = PrimeMLP(config.hidden_size, config.intermediate_size)
 
@@ -119,6 +124,8 @@ class PrimeForCausalLM(nn.Module):
             for layer in self.layers:
                 layer.self_attn.o_proj.weight.normal_(mean=0.0, std=scale)
                 layer.mlp.down_proj.weight.normal_(mean=0.0, std=scale)
+                if hasattr(layer.self_attn, "init_selective_weights"):
+                    layer.self_attn.init_selective_weights()
 
     def _init_weights(self, module: nn.Module):
         if isinstance(module, (nn.Linear, nn.Embedding)):
@@ -205,6 +212,8 @@ class DecodeGraph:
         h = m.embed_tokens(self.tokens)  # [B, 1, hidden]
         for layer, st in zip(m.layers, self.states):
             attn = layer.self_attn
+            if isinstance(attn, PrimeSelectiveMomentAttention):
+                raise NotImplementedError("DecodeGraph serves moment-attention layers; use generate() for selective")
             x = layer.input_layernorm(h)
             B = x.shape[0]
             H, D, Hk = attn.num_heads, attn.head_dim, attn.num_kv_heads

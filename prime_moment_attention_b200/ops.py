@@ -426,3 +426,91 @@ def delta_decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: t
                                   st_out.data_ptr(), ctypes.byref(ys), _stream(dev))
     _lib.check("pma_delta_decode_step", rc)
     return y, st_out
+
+
+# ---------------------------------------------------------------- selective variant
+def selective_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, log_decay: torch.Tensor,
+                      beta: torch.Tensor, state: Optional[StateTuple] = None, eps: float = 1.0,
+                      return_state: bool = True, out_dtype: Optional[torch.dtype] = None,
+                      y_out: Optional[torch.Tensor] = None, want_y: bool = True,
+                      prologue: Optional[Prologue] = None):
+    """Selective moment attention (PrimeSelectiveMomentAttention's core) over q (pre-scaled), k, v
+    [B,H,L,D] (k, v with H / kv_groups heads under a prologue); log_decay [B,H,L] = -Delta/tau;
+    beta [H].  States in the reference's selective layout.  Returns (y or None, state or None)."""
+    dev = _require_cuda(q, k, v)
+    if q.dim() != 4:
+        raise ValueError("q must be [B,H,L,D]")
+    B, H, L, D = q.shape
+    kv_shape = (B, _kv_heads(H, prologue), L, D)
+    if tuple(k.shape) != kv_shape or tuple(v.shape) != kv_shape:
+        raise ValueError(f"k, v must be {kv_shape}")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k, v must share one dtype")
+    L_ = _lib.load()
+    qs, q = _seq(q)
+    ks, k = _seq(k)
+    vs, v = _seq(v)
+    ld = _gate(log_decay, (B, H, L), dev, "log_decay")
+    bt = _gate(beta, (H,), dev, "beta")
+    st_in = None
+    if state is not None:
+        st_in_c, state = _state(state, B, H, D, "state")
+        st_in = ctypes.byref(st_in_c)
+    st_out_t = new_state(B, H, D, dev, zero=False) if return_state else None
+    st_out = ctypes.byref(_lib.State(*[t.data_ptr() for t in st_out_t])) if return_state else None
+    y = ys = None
+    if want_y:
+        if y_out is not None:
+            if tuple(y_out.shape) != (B, H, L, D) or not _seq_ok(y_out):
+                raise ValueError("y_out must be a [B,H,L,D] tensor with a contiguous, 16-byte aligned last axis")
+            y = y_out
+        else:
+            y = torch.empty(B, H, L, D, dtype=out_dtype or q.dtype, device=dev)
+        ys = ctypes.byref(_seq(y)[0])
+    pc, keep = (prologue.to_c(D, dev) if prologue is not None else (None, None))
+    rc = L_.pma_selective_prefill(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs),
+                                  ctypes.byref(pc) if pc is not None else None, ld.data_ptr(), bt.data_ptr(),
+                                  st_in, st_out, float(eps), ys, _stream(dev))
+    _lib.check("pma_selective_prefill", rc)
+    return y, st_out_t
+
+
+def selective_decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, log_decay: torch.Tensor,
+                          beta: torch.Tensor, state: StateTuple, eps: float = 1.0, inplace: bool = False,
+                          out_dtype: Optional[torch.dtype] = None, y_out: Optional[torch.Tensor] = None,
+                          prologue: Optional[Prologue] = None, rows: Optional[torch.Tensor] = None):
+    """Selective L == 1 step: q, k, v [N,H,D]; log_decay [N,H]; beta [H]; state in the selective
+    layout ([N,H,...], or a pool [P,H,...] with `rows`, updated in place).  Returns (y, state)."""
+    dev = _require_cuda(q, k, v)
+    N, H, D = _check_step_shapes(q, k, v, prologue)
+    L_ = _lib.load()
+    qs, q = _seq(q, False)
+    ks, k = _seq(k, False)
+    vs, v = _seq(v, False)
+    ld = _gate(log_decay, (N, H), dev, "log_decay")
+    bt = _gate(beta, (H,), dev, "beta")
+    P = state[0].shape[0] if rows is not None else N
+    st_in_c, st_in_t = _state(state, P, H, D, "state")
+    if inplace or rows is not None:
+        if not all(a.data_ptr() == b.data_ptr() for a, b in zip(st_in_t, state)):
+            raise ValueError("an in-place update needs contiguous float32 state tensors")
+        st_out_t = st_in_t
+    else:
+        st_out_t = new_state(N, H, D, dev, zero=False)
+    st_out_c = _lib.State(*[t.data_ptr() for t in st_out_t])
+    y = y_out if y_out is not None else torch.empty(N, H, D, dtype=out_dtype or q.dtype, device=dev)
+    ys, y2 = _seq(y, False)
+    if y2 is not y:
+        raise ValueError("y_out must have a contiguous, 16-byte aligned last axis")
+    if rows is not None:
+        if rows.dtype != torch.int32 or rows.dim() != 1 or rows.shape[0] != N or rows.device != dev:
+            raise ValueError("rows must be an int32 tensor [N] on the inputs' device")
+        rows = rows.contiguous()
+    pc, keep = (prologue.to_c(D, dev) if prologue is not None else (None, None))
+    rc = L_.pma_selective_decode_step(N, H, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs),
+                                      ctypes.byref(pc) if pc is not None else None, ld.data_ptr(), bt.data_ptr(),
+                                      rows.data_ptr() if rows is not None else None, P if rows is not None else 0,
+                                      ctypes.byref(st_in_c), ctypes.byref(st_out_c), float(eps), ctypes.byref(ys),
+                                      _stream(dev))
+    _lib.check("pma_selective_decode_step", rc)
+    return y, st_out_t

@@ -6,13 +6,16 @@ which keeps the reference's projection / QK-norm / scale code and sends all thre
 L branches to libpma.so.  The state tuple format is unchanged, so
 PrimeMomentCache and PrimeForCausalLM (model.py:101-120, 203-242) work as they are.
 `install(ChunkedGatedDeltaPrimeAttention)` does the same for the reference's gated
-delta-rule module (chunked_delta_prime.py:89-283) with delta.delta_forward.
+delta-rule module (chunked_delta_prime.py:89-283) with delta.delta_forward, and
+`install(PrimeSelectiveMomentAttention)` for the selective module (selective.py:264-444) with
+selective.selective_forward.
 `uninstall()` restores the original forward.
 """
 from __future__ import annotations
 
 from .attention import moment_forward
 from .delta import delta_forward
+from .selective import selective_forward
 
 _saved: dict = {}
 
@@ -24,9 +27,13 @@ def _default_cls():
 
 def _forward_for(cls):
     """The kernel forward for a reference class: the gated delta-rule module
-    (chunked_delta_prime.py) has its own state format and core; everything else is the
-    moment-attention forward."""
-    return delta_forward if hasattr(cls, "_build_features") or "Delta" in cls.__name__ else moment_forward
+    (chunked_delta_prime.py) and the selective module (selective.py) have their own cores;
+    everything else is the moment-attention forward."""
+    if hasattr(cls, "_build_features") or "Delta" in cls.__name__:
+        return delta_forward
+    if hasattr(cls, "get_tau") or "Selective" in cls.__name__:
+        return selective_forward
+    return moment_forward
 
 
 def install(cls=None):

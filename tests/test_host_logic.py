@@ -161,3 +161,35 @@ def test_delta_module_parameters_match_reference_layout():
                       "q_norm.bias": (16,), "k_norm.weight": (16,), "k_norm.bias": (16,)}
     assert torch.all(m.erase_proj.bias == -2.5) and torch.all(m.write_proj.bias == -1.0)
     assert (m.chunk_size, m.decay, m.lyapunov_bound, m.eps, m.num_kv_groups) == (64, 0.9995, 25.0, 1e-5, 2)
+
+
+class SelectiveStandIn(nn.Module):
+    """Has the selective module's get_tau (selective.py:344-345)."""
+
+    def get_tau(self, device):
+        return None
+
+    def forward(self, hidden_states, state=None, return_state=False):
+        return "original", None
+
+
+def test_install_picks_the_selective_forward():
+    pma.install(SelectiveStandIn)
+    try:
+        assert SelectiveStandIn.forward is pma.selective_forward
+    finally:
+        pma.uninstall(SelectiveStandIn)
+
+
+def test_selective_module_parameters_and_identity_init():
+    """Parameters of selective.py:299-320 and the identity-preserving init of :322-330."""
+    m = pma.PrimeSelectiveMomentAttention(hidden_size=64, num_heads=4, head_dim=16, decay=0.99)
+    assert {n: tuple(p.shape) for n, p in m.named_parameters()} == {
+        "q_proj.weight": (64, 64), "k_proj.weight": (64, 64), "v_proj.weight": (64, 64), "o_proj.weight": (64, 64),
+        "q_norm.weight": (16,), "q_norm.bias": (16,), "k_norm.weight": (16,), "k_norm.bias": (16,),
+        "delta_proj.weight": (4, 64), "delta_proj.bias": (4,), "log_tau": (4,), "log_beta": (4,)}
+    x = torch.randn(2, 5, 64)
+    delta = torch.nn.functional.softplus(m.delta_proj(x))
+    lam = torch.exp(-delta / m.get_tau(torch.device("cpu")))
+    assert torch.allclose(lam, torch.full_like(lam, 0.99), atol=1e-6)
+    assert torch.all(m.get_beta(torch.device("cpu")) == 1.0)
