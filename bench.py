@@ -10,7 +10,8 @@ pma_prefill call over that batch (y and the final state).  The line also carries
 the config-3 decode step (256 sequences x 12 layers x 12 heads, D=64, one launch
 for all layers' heads, 1000 timed steps) under "decode", and the gated delta-rule variant
 (config-2 prefill with the write gate beta, and its decode step at the config-3 shape) under
-"delta", and the config-4 model (prefill and CUDA-graph decode) under "model".
+"delta", the selective variant under "selective", the config-4 model (prefill and CUDA-graph decode)
+under "model", and the config-5 long sequence (sequence shards over the GPUs) under "sp".
 
 Multi-GPU: one process per GPU (torchrun); each rank prefills its own batch x head
 shard with no collective (weak scaling); times are the max over ranks.
@@ -493,6 +494,130 @@ def bench_model(args, ws, rank, device, stream, peaks):
             "gpu_launches": None, "clocks": clk_r}
 
 
+SP = dict(B=1, H=16, D=128, L=1 << 20, lam=(0.999, 0.99995), seed=6)
+SP_FLOP_PER_TOKHEAD = 6 * 64 * 128 + 8 * 128 * 128   # SURVEY-style count at C = 64, D = 128: 180,224
+SP_BYTES_PER_TOKHEAD = 8 * 128                         # q, k, v in + y out, bf16
+
+
+def bench_sp(args, ws, rank, device, stream, peaks):
+    """Config 5: one sequence of 2^20 tokens, H = 16, D = 128, bf16, split into ws contiguous
+    shards (one per rank): a state-only pass per shard, an NCCL all-gather of the shard states,
+    the decay-weighted prefix fold and the full pass from the carried state
+    (sp.sequence_parallel_prefill).  With one GPU, one pma_prefill over the whole sequence (the
+    same carry runs across CTAs as segments).  Total work is fixed: strong scaling."""
+    import torch
+    from prime_moment_attention_b200 import ops, sp, synth
+    hbm_peak, _, peak_kind = peaks
+    c = SP
+    Ls = c["L"] // ws
+    q, k, v = synth.make_qkv(c["B"], c["H"], Ls, c["D"], seed=c["seed"] + 1000 * rank, dtype=torch.bfloat16,
+                             device=device)
+    lam = synth.make_lambdas(c["H"], *c["lam"], seed=c["seed"]).to(device)
+    y = torch.empty_like(q)
+    if ws == 1:
+        def step():
+            ops.prefill(q, k, v, lam, y_out=y, return_state=True)
+    else:
+        def step():
+            sp.sequence_parallel_prefill(q, k, v, lam, y_out=y, shard_lengths=[Ls] * ws)
+    steps = max(3, min(args.steps, 5))
+    clk = ClockSampler(device.index)
+    clk.start()
+    ms = max_over_ranks(time_steps(step, steps, 3, ws, device, stream), ws, device)
+    clk_r = clk.stop()
+    tokheads = c["B"] * c["L"] * c["H"]
+    tf = tokheads * SP_FLOP_PER_TOKHEAD / (ms * 1e-3) / 1e12
+    bw = tokheads * SP_BYTES_PER_TOKHEAD / (ms * 1e-3) / 1e9
+    return {"metric": "sp_prefill_tok_per_s", "value": round(c["B"] * c["L"] / (ms * 1e-3), 1), "unit": "tok/s",
+            "ms_per_step": round(ms, 3), "steps": steps, "higher_is_better": True, "scaling": "strong",
+            "dtype": "bf16 in, fp32 math",
+            "config": {"workload": "config5 long-sequence prefill: B=1, H=16, D=128, L=2^20 bf16, per-head lambda "
+                                   f"log-U[0.999,0.99995], {ws} contiguous shard(s) of {Ls} tokens",
+                       "path": "pma_prefill (CUDA cores at D=128, segments across CTAs)" if ws == 1 else
+                               "sequence_parallel_prefill: state-only pass, NCCL all_gather, prefix fold, full pass"},
+            "roofline": {"bound": "fp32 CUDA cores", "achieved": round(tf, 2), "peak": round(FP32_SIMT_PEAK_TFLOPS, 1),
+                         "unit": "TFLOP/s", "frac": round(tf / FP32_SIMT_PEAK_TFLOPS, 4), "traffic": None,
+                         "peak_kind": "nominal (148 SMs x 128 FMA/clk x 1965 MHz) per GPU x " + str(ws),
+                         "hbm": {"achieved": round(bw, 1), "peak": hbm_peak * ws, "unit": "GB/s",
+                                 "frac": round(bw / (hbm_peak * ws), 4), "peak_kind": peak_kind},
+                         "algorithmic_flop_per_step": tokheads * SP_FLOP_PER_TOKHEAD},
+            "gpu_launches": None, "clocks": clk_r}
+
+
+SEL_FLOP_PER_TOKHEAD = 6 * 64 * 64 + 8 * 64 * 64  # chunk form at C = 64 on CUDA cores: 57,344
+
+
+def bench_selective(args, ws, rank, device, stream, peaks):
+    """Selective variant at the config-2 shape (per-token decay exp(-Delta_t / tau_h) with
+    Delta_t = softplus(N(0,1)), tau_h log-U[2, 2000], beta_h = exp(0.4 N(0,1))) and its decode step
+    at the config-3 shape."""
+    import torch
+    import torch.nn.functional as F
+    from prime_moment_attention_b200 import ops, synth
+    hbm_peak, _, peak_kind = peaks
+    c = PREFILL
+    B, H, L, D = args.prefill_batch or c["B"], c["H"], c["L"], c["D"]
+    q, k, v = synth.make_qkv(B, H, L, D, seed=c["seed"] + 1000 * rank, dtype=torch.bfloat16, device=device)
+    g = torch.Generator(device=device).manual_seed(c["seed"] + 31 + rank)
+    tau = torch.exp(torch.empty(H, device=device).uniform_(math.log(2.0), math.log(2000.0), generator=g))
+    ld = (-F.softplus(torch.randn(B, H, L, device=device, generator=g)) / tau.view(1, H, 1)).contiguous()
+    beta = torch.exp(0.4 * torch.randn(H, device=device, generator=g)).clamp(0.1, 15.0)
+    y = torch.empty_like(q)
+
+    def step():
+        ops.selective_prefill(q, k, v, ld, beta, y_out=y, return_state=True)
+
+    steps = max(3, min(args.steps, 10))
+    clk = ClockSampler(device.index)
+    clk.start()
+    ms = max_over_ranks(time_steps(step, steps, args.warmup, ws, device, stream), ws, device)
+    clk_r = clk.stop()
+    tokheads = B * L * H
+    tf = tokheads * SEL_FLOP_PER_TOKHEAD / (ms * 1e-3) / 1e12
+    pre = {"metric": "selective_prefill_tok_per_s", "value": round(B * L * ws / (ms * 1e-3), 1), "unit": "tok/s",
+           "ms_per_step": round(ms, 4), "steps": steps, "higher_is_better": True, "dtype": "bf16 in, fp32 math",
+           "config": {"workload": "config2-shape selective prefill: B=8 seqs/GPU, H=12, D=64, L=8192, bf16 q/k/v, "
+                                  "per-token decay exp(-softplus(N(0,1))/tau_h), tau_h log-U[2,2000]"},
+           "roofline": {"bound": "fp32 CUDA cores", "achieved": round(tf, 2), "peak": round(FP32_SIMT_PEAK_TFLOPS, 1),
+                        "unit": "TFLOP/s", "frac": round(tf / FP32_SIMT_PEAK_TFLOPS, 4), "traffic": None,
+                        "peak_kind": "nominal (148 SMs x 128 FMA/clk x 1965 MHz)",
+                        "algorithmic_flop_per_launch": tokheads * SEL_FLOP_PER_TOKHEAD},
+           "gpu_launches": steps, "clocks": clk_r}
+    del q, k, v, y, ld
+    torch.cuda.empty_cache()
+    dc = DECODE
+    N, HD = dc["seqs"], dc["layers"] * dc["H"]
+    lam_d = synth.make_lambdas(HD, *dc["lam"], seed=dc["seed"]).to(device)
+    st = synth.make_state(N, HD, D, lam_d, seed=dc["seed"] + rank, t0=dc["t0"], sigma=dc["sigma"], device=device)
+    toks = [synth.make_decode_tokens(N, HD, D, seed=dc["seed"] * 100 + i, device=device) for i in range(8)]
+    ldd = (-F.softplus(torch.randn(N, HD, device=device, generator=g)) / 500.0).contiguous()
+    bd = torch.exp(0.4 * torch.randn(HD, device=device, generator=g)).clamp(0.1, 15.0)
+    yd = torch.empty(N, HD, D, dtype=torch.bfloat16, device=device)
+    it = [0]
+
+    def dstep():
+        qq, kk, vv = toks[it[0] & 7]
+        it[0] += 1
+        ops.selective_decode_step(qq, kk, vv, ldd, bd, st, inplace=True, y_out=yd)
+
+    dsteps = min(args.decode_steps or 200, 200)
+    dclk = ClockSampler(device.index)
+    dclk.start()
+    dms = max_over_ranks(time_steps(dstep, dsteps, max(3, args.warmup), ws, device, stream), ws, device)
+    dclk_r = dclk.stop()
+    d_bytes = N * HD * (DECODE_BYTES_PER_HEADSTEP + 4)
+    d_bw = d_bytes / (dms * 1e-3) / 1e9
+    dec = {"metric": "selective_decode_step_us", "value": round(dms * 1e3, 2), "unit": "us/step",
+           "higher_is_better": False, "steps": dsteps,
+           "config": {"workload": "config3-shape selective decode: 256 seqs x 12 layers x 12 heads, D=64, "
+                                  "per-token decay, fp32 state in place"},
+           "roofline": {"bound": "hbm", "achieved": round(d_bw, 1), "peak": hbm_peak, "unit": "GB/s",
+                        "frac": round(d_bw / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+                        "algorithmic_bytes_per_launch": d_bytes},
+           "gpu_launches": dsteps, "clocks": dclk_r}
+    return {"prefill": pre, "decode": dec}
+
+
 def run_ours(args):
     import torch
     ws, rank, local = dist_setup()
@@ -518,6 +643,21 @@ def run_ours(args):
             line["model"] = md
         else:
             line = dict(md, n_gpus=ws, warmup=args.warmup, data="synthetic", vs_baseline=None)
+        torch.cuda.empty_cache()
+    if args.workload in ("both", "sp"):
+        spl = bench_sp(args, ws, rank, device, stream, peaks)
+        if line:
+            line["sp"] = spl
+        else:
+            line = dict(spl, n_gpus=ws, warmup=args.warmup, data="synthetic", vs_baseline=None)
+        torch.cuda.empty_cache()
+    if args.workload in ("both", "selective"):
+        sl = bench_selective(args, ws, rank, device, stream, peaks)
+        if line:
+            line["selective"] = sl
+        else:
+            line = dict(sl["prefill"], n_gpus=ws, warmup=args.warmup, scaling="weak", data="synthetic",
+                        vs_baseline=None, selective_decode=sl["decode"])
         torch.cuda.empty_cache()
     if args.workload in ("both", "delta"):
         dl = bench_delta(args, ws, rank, device, stream, peaks)
@@ -555,7 +695,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["both", "prefill", "decode", "delta", "model"], default="both",
+    ap.add_argument("--workload", choices=["both", "prefill", "decode", "delta", "model", "selective", "sp"], default="both",
                     help="profiling aid: run only one part (the JSON line then lacks the others)")
     ap.add_argument("--prefill-batch", type=int, default=0,
                     help="profiling aid: sequences per GPU for the prefill part (default: config 2's 8)")
