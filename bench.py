@@ -122,6 +122,9 @@ def dist_setup():
     if ws > 1:
         import datetime
         import torch.distributed as dist
+        # NCCL's own log lines (its version banner under NCCL_DEBUG=VERSION) go to stderr, so that
+        # rank 0's stdout carries the one JSON line only
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
