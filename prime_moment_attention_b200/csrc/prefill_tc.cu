@@ -708,8 +708,7 @@ __global__ void __launch_bounds__(512, 1)
         // only this quadrant reads: a helper stores after the owner has its At blocks in registers.
         if (!SO) {
             const int wq = warp & 3;
-            const bool helper = warp < 4;
-            const int i = wq * 32 + lane;
+            const bool helper = warp < 4;  // this thread's P row is wq * 32 + lane
             const uint32_t lane_base = tmem + ((uint32_t)(wq * 32) << 16);
             const int nq = 2 * wq + 2;                                   // nonzero blocks of the quadrant
             const int split = wq == 2 ? 3 : (wq == 3 ? 4 : nq);          // first block of the helper
