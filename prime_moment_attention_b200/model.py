@@ -195,6 +195,13 @@ class DecodeGraph:
         self.model = model
         dev = tokens.device
         self.states = [tuple(t.detach().to(torch.float32).contiguous().clone() for t in st) for st in states]
+        # one GEMM for q, k, v and one for gate, up per layer (concatenated copies of the weights,
+        # taken now: the graph serves the weights as they are at construction)
+        self.w_qkv, self.w_gu = [], []
+        for layer in model.layers:
+            a, mlp = layer.self_attn, layer.mlp
+            self.w_qkv.append(torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight]).detach().contiguous())
+            self.w_gu.append(torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight]).detach().contiguous())
         self.tokens = tokens.detach().reshape(-1, 1).clone()
         self.logits = None
         s = torch.cuda.Stream(dev)
@@ -210,16 +217,18 @@ class DecodeGraph:
     def _body(self, write: bool):
         m = self.model
         h = m.embed_tokens(self.tokens)  # [B, 1, hidden]
-        for layer, st in zip(m.layers, self.states):
+        h = h[:, 0]  # [B, hidden]
+        for layer, st, w_qkv, w_gu in zip(m.layers, self.states, self.w_qkv, self.w_gu):
             attn = layer.self_attn
             if isinstance(attn, PrimeSelectiveMomentAttention):
                 raise NotImplementedError("DecodeGraph serves moment-attention layers; use generate() for selective")
             x = layer.input_layernorm(h)
             B = x.shape[0]
             H, D, Hk = attn.num_heads, attn.head_dim, attn.num_kv_heads
-            q = attn.q_proj(x).view(B, H, D)
-            k = attn.k_proj(x).view(B, Hk, D)
-            v = attn.v_proj(x).view(B, Hk, D)
+            qkv = torch.mm(x, w_qkv.t())  # [B, (H + 2 Hk) D]; q, k, v are strided views of it
+            q = qkv[:, :H * D].view(B, H, D)
+            k = qkv[:, H * D:(H + Hk) * D].view(B, Hk, D)
+            v = qkv[:, (H + Hk) * D:].view(B, Hk, D)
             decay = getattr(attn, "decay_per_head", None)
             decay = attn.decay if decay is None else decay
             pro = _prologue(attn)
@@ -227,9 +236,11 @@ class DecodeGraph:
                 raise NotImplementedError("DecodeGraph needs QK-norms the kernels fold (nn.LayerNorm over head_dim)")
             y, _ = ops.decode_step(q, k, v, decay, st if write else tuple(t.clone() for t in st), eps=attn.eps,
                                    inplace=True, prologue=pro)
-            h = h + attn.o_proj(y.reshape(B, 1, H * D).to(h.dtype))
-            h = h + layer.mlp(layer.post_attention_layernorm(h))
-        logits = m.lm_head(m.norm(h))[:, -1, :]
+            h = torch.addmm(h, y.reshape(B, H * D).to(h.dtype), attn.o_proj.weight.t())  # residual + o_proj
+            gu = torch.mm(layer.post_attention_layernorm(h), w_gu.t())
+            inter = gu.shape[1] // 2
+            h = torch.addmm(h, F.silu(gu[:, :inter]) * gu[:, inter:], layer.mlp.down_proj.weight.t())
+        logits = m.lm_head(m.norm(h))
         nxt = torch.argmax(logits, dim=-1, keepdim=True)
         if write:
             self.logits = logits
