@@ -547,9 +547,6 @@ def bench_sp(args, ws, rank, device, stream, peaks):
             "gpu_launches": None, "clocks": clk_r}
 
 
-SEL_FLOP_PER_TOKHEAD = 6 * 64 * 64 + 8 * 64 * 64  # chunk form at C = 64 on CUDA cores: 57,344
-
-
 def bench_selective(args, ws, rank, device, stream, peaks):
     """Selective variant at the config-2 shape (per-token decay exp(-Delta_t / tau_h) with
     Delta_t = softplus(N(0,1)), tau_h log-U[2, 2000], beta_h = exp(0.4 N(0,1))) and its decode step
@@ -576,15 +573,19 @@ def bench_selective(args, ws, rank, device, stream, peaks):
     ms = max_over_ranks(time_steps(step, steps, args.warmup, ws, device, stream), ws, device)
     clk_r = clk.stop()
     tokheads = B * L * H
-    tf = tokheads * SEL_FLOP_PER_TOKHEAD / (ms * 1e-3) / 1e12
+    bw = tokheads * (PREFILL_BYTES_PER_TOKHEAD + 4) / (ms * 1e-3) / 1e9  # + the fp32 log decay per token-head
+    tf = tokheads * PREFILL_FLOP_PER_TOKHEAD / (ms * 1e-3) / 1e12
     pre = {"metric": "selective_prefill_tok_per_s", "value": round(B * L * ws / (ms * 1e-3), 1), "unit": "tok/s",
-           "ms_per_step": round(ms, 4), "steps": steps, "higher_is_better": True, "dtype": "bf16 in, fp32 math",
+           "ms_per_step": round(ms, 4), "steps": steps, "higher_is_better": True, "dtype": "bf16",
            "config": {"workload": "config2-shape selective prefill: B=8 seqs/GPU, H=12, D=64, L=8192, bf16 q/k/v, "
-                                  "per-token decay exp(-softplus(N(0,1))/tau_h), tau_h log-U[2,2000]"},
-           "roofline": {"bound": "fp32 CUDA cores", "achieved": round(tf, 2), "peak": round(FP32_SIMT_PEAK_TFLOPS, 1),
-                        "unit": "TFLOP/s", "frac": round(tf / FP32_SIMT_PEAK_TFLOPS, 4), "traffic": None,
-                        "peak_kind": "nominal (148 SMs x 128 FMA/clk x 1965 MHz)",
-                        "algorithmic_flop_per_launch": tokheads * SEL_FLOP_PER_TOKHEAD},
+                                  "per-token decay exp(-softplus(N(0,1))/tau_h), tau_h log-U[2,2000], beta_h "
+                                  "exp(0.4 N(0,1)); tensor cores (head-states with a chunk decaying past e^-76 "
+                                  "run the float32 loop)"},
+           "roofline": {"bound": "hbm", "achieved": round(bw, 1), "peak": hbm_peak, "unit": "GB/s",
+                        "frac": round(bw / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+                        "tensor": {"achieved": round(tf, 1), "peak": peaks[1], "unit": "TFLOP/s",
+                                   "frac": round(tf / peaks[1], 4)},
+                        "algorithmic_bytes_per_launch": tokheads * (PREFILL_BYTES_PER_TOKHEAD + 4)},
            "gpu_launches": steps, "clocks": clk_r}
     del q, k, v, y, ld
     torch.cuda.empty_cache()

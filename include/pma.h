@@ -342,13 +342,20 @@ PMA_API int pma_delta_decode_step(int N, int H, int D,
  *   log_decay   device float [B,H,L] contiguous: -Delta_t / tau_h.
  *   beta        device float [H]: the temperature (clamp(exp(log_beta), 0.1, 15) in the module).
  *   prologue    as pma_prefill_ex (GQA map, QK-norm, q scale) or NULL.
- * Computed in float32 on CUDA cores for every D in {16, 32, 64, 128} and both input dtypes.
+ *   workspace   at least pma_selective_prefill_workspace_bytes(...) bytes (256 for the tensor-core
+ *               path, plus the normalised rows when the prologue has LayerNorms; 0 otherwise).
+ * BF16 inputs with D = 64 run on tcgen05 tensor cores (per-chunk exp(+-cumulative log decay)
+ * factors in place of the per-head powers; head-states with a chunk that decays by more than
+ * e^-76 run the float32 loop); float32 inputs and other D run in float32 on CUDA cores.
  */
+PMA_API size_t pma_selective_prefill_workspace_bytes(int B, int H, int L, int D, int dtype,
+                                                     const pma_prologue *prologue);
 PMA_API int pma_selective_prefill(int B, int H, int L, int D,
                                   const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
                                   const pma_prologue *prologue, const float *log_decay, const float *beta,
                                   const pma_state *state_in, const pma_state *state_out,
-                                  float eps, const pma_seq_tensor *y, pma_stream_t stream);
+                                  float eps, const pma_seq_tensor *y,
+                                  void *workspace, size_t workspace_bytes, pma_stream_t stream);
 
 /*
  * Selective decode step (the L == 1 branch, selective.py:367-396): log_decay [N,H]

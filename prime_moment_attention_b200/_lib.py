@@ -109,9 +109,12 @@ def load() -> ctypes.CDLL:
                                         + [ctypes.c_float] * 2 + [ctypes.c_void_p] * 2
                                         + [_P(SeqTensor), ctypes.c_void_p])
     L.pma_delta_decode_step.restype = ctypes.c_int
+    L.pma_selective_prefill_workspace_bytes.argtypes = [ctypes.c_int] * 5 + [_P(Prologue)]
+    L.pma_selective_prefill_workspace_bytes.restype = ctypes.c_size_t
     L.pma_selective_prefill.argtypes = ([ctypes.c_int] * 4 + [_P(SeqTensor)] * 3 + [_P(Prologue)]
                                         + [ctypes.c_void_p] * 2 + [_P(State)] * 2
-                                        + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p])
+                                        + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p, ctypes.c_size_t,
+                                           ctypes.c_void_p])
     L.pma_selective_prefill.restype = ctypes.c_int
     L.pma_selective_decode_step.argtypes = ([ctypes.c_int] * 3 + [_P(SeqTensor)] * 3 + [_P(Prologue)]
                                             + [ctypes.c_void_p] * 2 + [ctypes.c_void_p, ctypes.c_int]

@@ -185,6 +185,43 @@ ProPass pro_pass(const Plan &pl, const Prologue &pro, int B, int H, int L, bool 
     return r;
 }
 
+// Tensor-core path: the QK-norm pass for q and / or k (pro_pass says which) into the workspace;
+// the core then reads the normalised rows and keeps the GQA map and a bf16-exact q scale.
+cudaError_t run_prologue_passes(const ProPass &pp, const Prologue &pro, PrefillParams &p, int B, int H, int L,
+                                void *workspace, bool want_y, int sms, cudaStream_t st) {
+    char *wsb = reinterpret_cast<char *>(workspace);
+    const int hkv = H / pro.groups;
+    cudaError_t e;
+    if (pp.q) {
+        if ((e = launch_qk_norm(p.q, B, H, L, pro.qw, pro.qb, pro.ln_eps, pro.q_scale, wsb + pp.q_off, sms, st)) !=
+            cudaSuccess)
+            return e;
+        p.q = Seq{wsb + pp.q_off, (int64_t)H * L * 64, (int64_t)L * 64, 64};
+        p.pro.q_scale = 1.0f;
+    }
+    if (pp.k) {
+        if ((e = launch_qk_norm(p.k, B, hkv, L, pro.kw, pro.kb, pro.ln_eps, 1.0f, wsb + pp.k_off, sms, st)) !=
+            cudaSuccess)
+            return e;
+        p.k = Seq{wsb + pp.k_off, (int64_t)hkv * L * 64, (int64_t)L * 64, 64};
+    }
+    p.pro.qw = p.pro.qb = p.pro.kw = p.pro.kb = nullptr;
+    if (!want_y) p.pro.q_scale = 1.0f;
+    return cudaSuccess;
+}
+
+// The selective prefill's plan: one segment per head-state (its per-token decay has no per-head
+// carry factor for the segment prefix); tensor cores for bf16 at D = 64.
+Plan selective_plan(int L, int D, int dtype) {
+    Plan p;
+    p.tc = tc_supported(D, dtype);
+    p.chunk = p.tc ? TC_CHUNK : simt_chunk(D);
+    p.nseg = 1;
+    p.seg_len = ((L + p.chunk - 1) / p.chunk) * p.chunk;
+    p.ws_bytes = p.tc ? WS_HEADER : 0;
+    return p;
+}
+
 cudaError_t launch_prefill(const Plan &pl, const PrefillParams &p, int D, int idt, int ydt, dim3 grid,
                            cudaStream_t st) {
     return pl.tc ? launch_prefill_tc(p, ydt, grid, st) : launch_prefill_simt(p, D, idt, ydt, grid, st);
@@ -341,23 +378,8 @@ int prefill_impl(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_
     p.v = seq_of(v);
     p.pro = pro;
     cudaError_t e;
-    if (pl.tc) {  // norms (and a scale bf16 cannot hold) by the QK-norm pass; the core keeps the GQA map
-        char *wsb = reinterpret_cast<char *>(workspace);
-        const int hkv = H / pro.groups;
-        if (pp.q) {
-            e = launch_qk_norm(p.q, B, H, L, pro.qw, pro.qb, pro.ln_eps, pro.q_scale, wsb + pp.q_off, di.sms, st);
-            if (e != cudaSuccess) return cuda_fail(e);
-            p.q = Seq{wsb + pp.q_off, (int64_t)H * L * 64, (int64_t)L * 64, 64};
-            p.pro.q_scale = 1.0f;
-        }
-        if (pp.k) {
-            e = launch_qk_norm(p.k, B, hkv, L, pro.kw, pro.kb, pro.ln_eps, 1.0f, wsb + pp.k_off, di.sms, st);
-            if (e != cudaSuccess) return cuda_fail(e);
-            p.k = Seq{wsb + pp.k_off, (int64_t)hkv * L * 64, (int64_t)L * 64, 64};
-        }
-        p.pro.qw = p.pro.qb = p.pro.kw = p.pro.kb = nullptr;
-        if (!y) p.pro.q_scale = 1.0f;
-    }
+    if (pl.tc && (e = run_prologue_passes(pp, pro, p, B, H, L, workspace, y != nullptr, di.sms, st)) != cudaSuccess)
+        return cuda_fail(e);
     p.y = seqout_of(y);
     p.lambda = lambda;
     p.lam_sb = lambda_stride_b;
@@ -528,10 +550,17 @@ int pma_delta_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pm
     return e == cudaSuccess ? PMA_OK : cuda_fail(e);
 }
 
+size_t pma_selective_prefill_workspace_bytes(int B, int H, int L, int D, int dtype, const pma_prologue *prologue) {
+    if (B <= 0 || H <= 0 || L <= 0 || !supported_d(D) || !supported_dtype(dtype)) return 0;
+    Prologue pro;
+    if (prologue_of(prologue, H, &pro) != PMA_OK) return 0;
+    return pro_pass(selective_plan(L, D, dtype), pro, B, H, L, true).total;
+}
+
 int pma_selective_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
                           const pma_seq_tensor *v, const pma_prologue *prologue, const float *log_decay,
                           const float *beta, const pma_state *state_in, const pma_state *state_out, float eps,
-                          const pma_seq_tensor *y, pma_stream_t stream) {
+                          const pma_seq_tensor *y, void *workspace, size_t workspace_bytes, pma_stream_t stream) {
     if (B < 0 || H <= 0 || L < 0 || !beta || (L > 0 && B > 0 && !log_decay)) return PMA_ERR_ARGUMENT;
     if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
     int rc;
@@ -567,11 +596,15 @@ int pma_selective_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, c
         }
         return PMA_OK;
     }
+    const Plan pl = selective_plan(L, D, q->dtype);
+    const ProPass pp = pro_pass(pl, pro, B, H, L, y != nullptr);
+    if (pp.total && (!workspace || workspace_bytes < pp.total)) return PMA_ERR_WORKSPACE;
+    if (pp.total && reinterpret_cast<uintptr_t>(workspace) % 16) return PMA_ERR_WORKSPACE;
     PrefillParams p{};
     p.B = B;
     p.H = H;
     p.L = L;
-    p.seg_len = ((L + simt_chunk(D) - 1) / simt_chunk(D)) * simt_chunk(D);
+    p.seg_len = pl.seg_len;
     p.q = seq_of(q);
     p.k = seq_of(k);
     p.v = seq_of(v);
@@ -587,7 +620,16 @@ int pma_selective_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, c
     p.logdecay = log_decay;
     p.k_head_scale = beta;
     p.half_sq = 1;
-    cudaError_t e = launch_prefill_simt(p, D, q->dtype, y ? y->dtype : PMA_F32, dim3(BH, 1), st);
+    cudaError_t e;
+    if (pl.tc) {
+        p.status = reinterpret_cast<int *>(workspace);
+        if ((e = cudaMemsetAsync(p.status, 0, sizeof(int), st)) != cudaSuccess) return cuda_fail(e);
+        if ((e = run_prologue_passes(pp, pro, p, B, H, L, workspace, y != nullptr, di.sms, st)) != cudaSuccess)
+            return cuda_fail(e);
+        e = launch_prefill_tc(p, y ? y->dtype : PMA_F32, dim3(BH, 1), st);
+    } else {
+        e = launch_prefill_simt(p, D, q->dtype, y ? y->dtype : PMA_F32, dim3(BH, 1), st);
+    }
     return e == cudaSuccess ? PMA_OK : cuda_fail(e);
 }
 

@@ -17,6 +17,13 @@
 // The rescaling keeps every factor inside float32/bf16 range for l >= 0.55
 // (l^-128 < 2e33, l^127 > 1e-33); head-states with a smaller decay run the
 // float32 CUDA-core chunk loop (prefill_simt_body.cuh) inside this kernel.
+// Per-token decay (PT, the selective variant): with c_i the chunk's inclusive prefix sum of
+// log lambda_t, the factors become g_i = exp(c_i), w_j = exp(c_{n-1} - c_j), l^-(1+j) -> exp(-c_j),
+// l^-n -> exp(-c_{n-1}), l^n -> exp(c_{n-1}); every role that needs them scans the chunk's log
+// decays itself (one warp scan, loaded a chunk ahead), so no new synchronisation is added.  A
+// head-state any of whose chunks decays by more than e^-76 (0.55^128) runs the CUDA-core loop.
+// k may carry a per-head temperature beta (KW = (w beta) k, K2W = (w beta^2) k^2) and the user
+// states the selective layout (S2, Z2 halved).
 //
 // The kernel is bound by shared-memory bandwidth (128 B/clk per SM, shared by
 // the tensor core's operand reads and every CUDA-core access), so the layout
@@ -71,6 +78,7 @@ constexpr int SB_SBO = 256;               // next 8-feature group
 constexpr int OFF_SMALL = OFF_SB + 5 * SB_LBO;
 constexpr int PREFETCH = 4;               // chunks of L2 prefetch ahead of the stage loads
 constexpr float LMIN = 0.55f;             // smallest decay the rescaled operands serve
+constexpr float LOGMIN = -76.0f;          // per-token decay: smallest chunk sum of log lambda served
 
 enum {
     B_FULL0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_PREP0, B_PREP1, B_PREP2,
@@ -89,6 +97,7 @@ struct Small {
     float z0f[4];                 // Z0 entering the chunk, by chunk mod 3
     uint32_t tmem_base;
     int abort_flag;
+    alignas(16) float cinv_pt[6][C];  // per-token decay: exp(-c_j) of the chunk, one row per mask warp
 };
 constexpr size_t SMEM_BYTES = OFF_SMALL + sizeof(Small) + 1024;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -378,11 +387,45 @@ __device__ __forceinline__ void store_row32<float>(float *dst, const float *v) {
     for (int c = 0; c < 8; ++c) d[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 }
 
+// ------------------------------------------------------------------ per-token decay helpers
+// log decays of chunk tokens 4 lane .. 4 lane + 3 (zero past n); scalar loads (any alignment)
+__device__ __forceinline__ float4 load_ld4(const float *ld, int t0, int n, int lane) {
+    const int i = 4 * lane;
+    return make_float4(i < n ? ld[t0 + i] : 0.f, i + 1 < n ? ld[t0 + i + 1] : 0.f, i + 2 < n ? ld[t0 + i + 2] : 0.f,
+                       i + 3 < n ? ld[t0 + i + 3] : 0.f);
+}
+
+// Inclusive prefix sums of the chunk's log decays: lane l receives c[m] = c_{4l+m}; returns c_{n-1}
+// (the chunk total: tokens past n add 0).  Whole warp.
+__device__ __forceinline__ float chunk_cum(float4 x, int lane, float c[4]) {
+    c[0] = x.x;
+    c[1] = c[0] + x.y;
+    c[2] = c[1] + x.z;
+    c[3] = c[2] + x.w;
+    float incl = c[3];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const float base = incl - c[3];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) c[m] += base;
+    return __shfl_sync(0xffffffffu, incl, 31);
+}
+
+// c_{4 src + m} held by lane src, selected by m (0..3)
+__device__ __forceinline__ float cum_at(const float c[4], int src, int m) {
+    const float v0 = __shfl_sync(0xffffffffu, c[0], src), v1 = __shfl_sync(0xffffffffu, c[1], src);
+    const float v2 = __shfl_sync(0xffffffffu, c[2], src), v3 = __shfl_sync(0xffffffffu, c[3], src);
+    return m == 0 ? v0 : (m == 1 ? v1 : (m == 2 ? v2 : v3));
+}
+
 // ------------------------------------------------------------------ the kernel
 // SO: state only (no q, no output rows).  PRO: q scaled by p.pro.q_scale as the prep warps load it
 // (the host uses this only when the scale is exact in bf16, so q * scale rounds as in float32;
 // LayerNorm prologues run as a separate pass before this kernel).
-template <bool SO, typename TO, bool PRO>
+template <bool SO, typename TO, bool PRO, bool PT>
 __global__ void __launch_bounds__(512, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                       const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
@@ -394,10 +437,24 @@ __global__ void __launch_bounds__(512, 1)
     const int bh = blockIdx.x, seg = blockIdx.y;
     const int b = bh / p.H, h = bh - b * p.H;
     const int hk = h / p.pro.groups;  // GQA: kv head of query head h
-    const float lam = p.lambda[(int64_t)b * p.lam_sb + h];
+    const float lam = PT ? 1.f : p.lambda[(int64_t)b * p.lam_sb + h];
+    const float *ldh = PT ? p.logdecay + (size_t)bh * p.L : nullptr;  // per-token log decays
 
-    if (!(lam >= LMIN)) {  // small decay (or NaN): float32 CUDA-core chunk loop, whole CTA
-        simt_prefill_body<64, 64, __nv_bfloat16, TO>(p, reinterpret_cast<float *>(smem), bh, seg);
+    bool small = !(lam >= LMIN);  // small decay (or NaN)
+    if (PT) {  // any chunk whose decay leaves the rescaled range (or NaN)
+        const int cb = seg * (p.seg_len / C), ce = min(cb + p.seg_len / C, (p.L + C - 1) / C);
+        int bad = 0;
+        for (int cc = cb + warp; cc < ce; cc += 16) {
+            const int t0 = cc * C, nn = min(C, p.L - t0);
+            float sum = 0.f;
+            for (int i = lane; i < nn; i += 32) sum += ldh[t0 + i];
+            sum = warp_sum(sum);
+            bad |= !(sum >= LOGMIN);
+        }
+        small = __syncthreads_or(bad) != 0;
+    }
+    if (small) {  // float32 CUDA-core chunk loop, whole CTA
+        simt_prefill_body<64, 64, __nv_bfloat16, TO, PT>(p, reinterpret_cast<float *>(smem), bh, seg);
         return;
     }
 
@@ -407,11 +464,12 @@ __global__ void __launch_bounds__(512, 1)
     const int c_end = min(c_begin + seg_chunks, nchunks_total);
     const int U = c_end - c_begin;
     const int n_last = min(C, p.L - (c_end - 1) * C);
+    const float kbeta = (PT && p.k_head_scale) ? p.k_head_scale[h] : 1.f;
     Ctl ctl{&sm.abort_flag, p.status};
 
     // ---- set-up: powers, barriers, tensor memory
-    if (threadIdx.x <= C) sm.pw[threadIdx.x] = (float)pow((double)lam, (double)threadIdx.x);
-    if (threadIdx.x < C) sm.cinv[threadIdx.x] = (float)pow((double)lam, -1.0 - (double)threadIdx.x);
+    if (!PT && threadIdx.x <= C) sm.pw[threadIdx.x] = (float)pow((double)lam, (double)threadIdx.x);
+    if (!PT && threadIdx.x < C) sm.cinv[threadIdx.x] = (float)pow((double)lam, -1.0 - (double)threadIdx.x);
     for (int i = threadIdx.x; i < TILE / 16; i += blockDim.x) {  // ones tile: row r = i / 8, chunk i % 8
         const int r = i >> 3, c = i & 7;
         const uint32_t one = (c == (r & 7)) ? 0x3F80u : 0u;  // element 0 of row r sits in chunk 0 ^ (r & 7)
@@ -442,7 +500,7 @@ __global__ void __launch_bounds__(512, 1)
     __syncthreads();
     tc_fence_after();
     fence_proxy_async();  // the ones tile is read by the tensor core
-    if (threadIdx.x == 0) {
+    if (!PT && threadIdx.x == 0) {
         float g = 0.f;
         for (int j = 0; j <= C; ++j) {
             sm.geo[j] = g;
@@ -588,9 +646,17 @@ __global__ void __launch_bounds__(512, 1)
         const int q_base = wp == 0 ? 0 : (wp == 1 ? 12 : (wp == 2 ? 20 : 28));  // first row quad of the warp
         const int nq_pass = wp == 0 ? 3 : (wp == 3 ? 1 : 2);                    // quads per thread
         const uint32_t lane_base = tmem + ((uint32_t)(wp * 32) << 16);
+        float4 ld_next = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (PT && U > 0) ld_next = load_ld4(ldh, c_begin * C, U == 1 ? n_last : C, lane);
         for (int u = 0, s = 0; u < U; ++u, s = (s == NST - 1) ? 0 : s + 1) {
             const int bb = u & 1;
             const int n = (u == U - 1) ? n_last : C;
+            float cpre[4], cend = 0.f;
+            if (PT) {  // this chunk's prefix sums; the next chunk's log decays are loaded now
+                const float4 x = ld_next;
+                if (u + 1 < U) ld_next = load_ld4(ldh, (c_begin + u + 1) * C, (u + 1 == U - 1) ? n_last : C, lane);
+                cend = chunk_cum(x, lane, cpre);
+            }
             if (!mbar_wait(&bar[B_FULL0 + s], (u / NST) & 1, ctl, 7)) break;
             uint8_t *k_s = smem + s * STAGE + OFF_K, *v_s = smem + s * STAGE + OFF_V, *k2_s = smem + s * STAGE + OFF_K2;
             uint4 xq[8];  // row tid of q, kept in registers until its tensor-memory buffer is free
@@ -614,10 +680,22 @@ __global__ void __launch_bounds__(512, 1)
                 // access then hit rows with four different swizzle phases (no bank conflicts)
                 const int rg = lane >> 3;
                 float wr[4];
+                if (PT) {
+                    const int src = r0 >> 2;  // lane holding c of rows r0 .. r0 + 3
+                    const float v0 = __shfl_sync(0xffffffffu, cpre[0], src), v1 = __shfl_sync(0xffffffffu, cpre[1], src);
+                    const float v2 = __shfl_sync(0xffffffffu, cpre[2], src), v3 = __shfl_sync(0xffffffffu, cpre[3], src);
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int r = r0 + ((t + rg) & 3);
-                    wr[t] = r < n ? sm.pw[n - 1 - r] : 0.f;
+                    for (int t = 0; t < 4; ++t) {
+                        const int mq = (t + rg) & 3;
+                        const float cv = mq == 0 ? v0 : (mq == 1 ? v1 : (mq == 2 ? v2 : v3));
+                        wr[t] = r0 + mq < n ? __expf(cend - cv) : 0.f;
+                    }
+                } else {
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const int r = r0 + ((t + rg) & 3);
+                        wr[t] = r < n ? sm.pw[n - 1 - r] : 0.f;
+                    }
                 }
                 uint4 x[4], y[4];
 #pragma unroll
@@ -630,15 +708,27 @@ __global__ void __launch_bounds__(512, 1)
                     const uint32_t e4[4] = {x[t].x, x[t].y, x[t].z, x[t].w};
                     const uint32_t v4[4] = {y[t].x, y[t].y, y[t].z, y[t].w};
                     const float2 w2 = make_float2(wr[t], wr[t]);
-                    const __nv_bfloat162 wb = __float2bfloat162_rn(wr[t]);
                     uint32_t o1[4], o2[4];
+                    if (PT) {  // KW = (w beta) k, K2W = (w beta^2) k^2
+                        const __nv_bfloat162 wb1 = __float2bfloat162_rn(wr[t] * kbeta);
+                        const __nv_bfloat162 wb2 = __float2bfloat162_rn(wr[t] * kbeta * kbeta);
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const __nv_bfloat162 kv = as_b2(e4[c]);
-                        const __nv_bfloat162 kw = __hmul2(kv, wb);
-                        o1[c] = as_u(kw);
-                        o2[c] = as_u(__hmul2(kw, kv));
-                        s0p[c] = __ffma2_rn(bf2f(v4[c]), w2, s0p[c]);
+                        for (int c = 0; c < 4; ++c) {
+                            const __nv_bfloat162 kv = as_b2(e4[c]);
+                            o1[c] = as_u(__hmul2(kv, wb1));
+                            o2[c] = as_u(__hmul2(__hmul2(kv, kv), wb2));
+                            s0p[c] = __ffma2_rn(bf2f(v4[c]), w2, s0p[c]);
+                        }
+                    } else {
+                        const __nv_bfloat162 wb = __float2bfloat162_rn(wr[t]);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const __nv_bfloat162 kv = as_b2(e4[c]);
+                            const __nv_bfloat162 kw = __hmul2(kv, wb);
+                            o1[c] = as_u(kw);
+                            o2[c] = as_u(__hmul2(kw, kv));
+                            s0p[c] = __ffma2_rn(bf2f(v4[c]), w2, s0p[c]);
+                        }
                     }
                     const uint32_t off = swz(r0 + ((t + rg) & 3), cc);
                     *reinterpret_cast<uint4 *>(k_s + off) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
@@ -715,10 +805,25 @@ __global__ void __launch_bounds__(512, 1)
             const int b0 = helper ? split : 0, nb = helper ? nq - split : split;
             const int zero_from = (wq == 2) ? (helper ? 48 : 64) : (wq < 2 ? 16 * wq + 16 : 64);
             uint64_t *mld = &bar[B_MLD0 + 2 * (wq - 2)];                 // quadrants 2, 3: [chunk parity]
+            float *const cwarp = sm.cinv_pt[helper ? 4 + (warp - 2) : warp - 8];  // per-token decay: this warp's
+            float4 ld_next = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (PT && U > 0) ld_next = load_ld4(ldh, c_begin * C, U == 1 ? n_last : C, lane);
             auto mask = [&](int u) -> bool {
                 const int bb = u & 1;
                 const int n = (u == U - 1) ? n_last : C;
-                const float cn = 1.0f / sm.pw[n];  // l^-n
+                float cn;
+                if (PT) {  // exp(-c_j) for the chunk's columns, into this warp's row of cinv_pt
+                    const float4 x = ld_next;
+                    if (u + 1 < U) ld_next = load_ld4(ldh, (c_begin + u + 1) * C, (u + 1 == U - 1) ? n_last : C, lane);
+                    float cc[4];
+                    const float cend = chunk_cum(x, lane, cc);
+                    *reinterpret_cast<float4 *>(cwarp + 4 * lane) =
+                        make_float4(__expf(-cc[0]), __expf(-cc[1]), __expf(-cc[2]), __expf(-cc[3]));
+                    __syncwarp();
+                    cn = __expf(-cend);
+                } else {
+                    cn = 1.0f / sm.pw[n];  // l^-n
+                }
                 const float2 cn2 = make_float2(cn, cn);
                 if (!mbar_wait(&bar[B_IFULL0 + bb], (u >> 1) & 1, ctl, 9)) return false;
                 tc_fence_after();
@@ -751,7 +856,7 @@ __global__ void __launch_bounds__(512, 1)
                 for (int j = 0; j < 4; ++j) {
                     if (j < nb) {
                         const int bk = b0 + j;
-                        const float4 *cv = reinterpret_cast<const float4 *>(sm.cinv + 16 * bk);
+                        const float4 *cv = reinterpret_cast<const float4 *>((PT ? cwarp : sm.cinv) + 16 * bk);
                         const int lim = lane - 16 * (bk - 2 * wq);  // column 16bk + c belongs to row i iff c <= lim
                         uint32_t pk[8];
 #pragma unroll
@@ -777,6 +882,7 @@ __global__ void __launch_bounds__(512, 1)
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&bar[B_PREADY0 + bb]);
+                if (PT) __syncwarp();  // every lane has read cwarp before the next chunk rewrites it
                 return true;
             };
             for (int u = 0; u < U; ++u)
@@ -804,6 +910,11 @@ __global__ void __launch_bounds__(512, 1)
                 for (int e = 0; e < D; ++e) S[e] = row[e];
             }
             Z = f < D ? src.Z1[f] : src.Z2[f - D];
+            if (PT && p.half_sq && f >= D && !p.in.packed) {  // selective layout: S2, Z2 held halved
+#pragma unroll
+                for (int e = 0; e < D; ++e) S[e] *= 2.f;
+                Z *= 2.f;
+            }
             if (f < D) s0 = src.S0[f];
             Z0 = src.Z0[0];
         } else {
@@ -833,13 +944,25 @@ __global__ void __launch_bounds__(512, 1)
         for (int u = 0, s = 0; u < U && ok; ++u, s = (s == NST - 1) ? 0 : s + 1) {
             const int bb = u & 1;
             const int n = (u == U - 1) ? n_last : C;
+            float decay = 0.f, zinc = 0.f, grow = 0.f;  // l^n, sum_j w_j, (PT) this output row's c
+            if (PT) {  // the log decays' load latency hides behind the waits below
+                const float4 x = load_ld4(ldh, (c_begin + u) * C, n, lane);
+                float cc[4];
+                const float cend = chunk_cum(x, lane, cc);
+                decay = __expf(cend);
+                float zs = 0.f;
+#pragma unroll
+                for (int m = 0; m < 4; ++m) zs += 4 * lane + m < n ? __expf(cend - cc[m]) : 0.f;
+                zinc = warp_sum(zs);
+                grow = cum_at(cc, f >> 2, f & 3);
+            }
             if (!mbar_wait(&bar[B_PREP0 + s], (u / NST) & 1, ctl, 11) ||
                 !mbar_wait(&bar[B_DSFULL0 + bb], (u >> 1) & 1, ctl, 12)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const float decay = sm.pw[n];
+            if (!PT) decay = sm.pw[n];
             const float2 dec2 = make_float2(decay, decay);
             float ds0 = 0.f;
             if (f < D) {
@@ -866,7 +989,7 @@ __global__ void __launch_bounds__(512, 1)
             }
             Z = fmaf(decay, Z, dz);
             if (f < D) s0 = fmaf(decay, s0, ds0);
-            Z0 = fmaf(decay, Z0, sm.geo[n]);
+            Z0 = fmaf(decay, Z0, PT ? zinc : sm.geo[n]);
             if (SO) continue;
             if (u + 1 < U) {
                 // the carry GEMM of chunk u has finished reading the state tile
@@ -887,7 +1010,7 @@ __global__ void __launch_bounds__(512, 1)
                 uint32_t r[32], r64;
                 tmem_ld33(lane_base + T_ACC, r, r64);  // columns 0..31 and the denominator column
                 const int s3 = u % 3;
-                const float g = sm.pw[f + 1];
+                const float g = PT ? __expf(grow) : sm.pw[f + 1];
                 const float den = __uint_as_float(r64) + sm.z0f[s3];  // carry + intra-chunk denominator
                 const float sc = g / fmaxf(g * den, p.eps);
                 const float2 sc2 = make_float2(sc, sc);
@@ -927,6 +1050,11 @@ __global__ void __launch_bounds__(512, 1)
         if (write_out) {
             const HeadPtrs dst = p.out.at(bh, p.out.packed ? seg : 0, D);
             float *row = f < D ? dst.S1 + f * D : dst.S2 + (f - D) * D;
+            if (PT && p.half_sq && f >= D && !p.out.packed) {  // selective layout: S2, Z2 halved
+#pragma unroll
+                for (int e = 0; e < D; ++e) S[e] *= 0.5f;
+                Z *= 0.5f;
+            }
             if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
 #pragma unroll
                 for (int e = 0; e < D; e += 4)
@@ -987,11 +1115,11 @@ static bool make_map(CUtensorMap *m, const Seq &s, int B, int H, int L) {
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool SO, typename TO, bool PRO>
+template <bool SO, typename TO, bool PRO, bool PT>
 static cudaError_t launch_t(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
                             const PrefillParams &p, dim3 grid, cudaStream_t st) {
-    auto kern = prefill_tc_kernel<SO, TO, PRO>;
-    cudaError_t e = set_smem_once<prefill_tc_kernel<SO, TO, PRO>>((int)SMEM_BYTES);
+    auto kern = prefill_tc_kernel<SO, TO, PRO, PT>;
+    cudaError_t e = set_smem_once<prefill_tc_kernel<SO, TO, PRO, PT>>((int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     kern<<<grid, 512, SMEM_BYTES, st>>>(mq, mk, mv, p);
     return cudaGetLastError();
@@ -1012,12 +1140,20 @@ cudaError_t launch_prefill_tc(const PrefillParams &p, int ydt, dim3 grid, cudaSt
     }
     const bool so = p.state_only || !p.y.p;
     if (p.pro.qw || p.pro.kw) return cudaErrorInvalidValue;  // norms are applied by the prologue pass
-    if (so) return tc::launch_t<true, float, false>(mq, mk, mv, p, grid, st);
+    if (p.logdecay) {  // per-token decay (one segment per head-state)
+        if (so) return tc::launch_t<true, float, false, true>(mq, mk, mv, p, grid, st);
+        if (p.pro.q_scale != 1.0f)
+            return ydt == PMA_F32 ? tc::launch_t<false, float, true, true>(mq, mk, mv, p, grid, st)
+                                  : tc::launch_t<false, __nv_bfloat16, true, true>(mq, mk, mv, p, grid, st);
+        return ydt == PMA_F32 ? tc::launch_t<false, float, false, true>(mq, mk, mv, p, grid, st)
+                              : tc::launch_t<false, __nv_bfloat16, false, true>(mq, mk, mv, p, grid, st);
+    }
+    if (so) return tc::launch_t<true, float, false, false>(mq, mk, mv, p, grid, st);
     if (p.pro.q_scale != 1.0f)
-        return ydt == PMA_F32 ? tc::launch_t<false, float, true>(mq, mk, mv, p, grid, st)
-                              : tc::launch_t<false, __nv_bfloat16, true>(mq, mk, mv, p, grid, st);
-    return ydt == PMA_F32 ? tc::launch_t<false, float, false>(mq, mk, mv, p, grid, st)
-                          : tc::launch_t<false, __nv_bfloat16, false>(mq, mk, mv, p, grid, st);
+        return ydt == PMA_F32 ? tc::launch_t<false, float, true, false>(mq, mk, mv, p, grid, st)
+                              : tc::launch_t<false, __nv_bfloat16, true, false>(mq, mk, mv, p, grid, st);
+    return ydt == PMA_F32 ? tc::launch_t<false, float, false, false>(mq, mk, mv, p, grid, st)
+                          : tc::launch_t<false, __nv_bfloat16, false, false>(mq, mk, mv, p, grid, st);
 }
 
 }  // namespace pma

@@ -468,9 +468,12 @@ def selective_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, log_dec
             y = torch.empty(B, H, L, D, dtype=out_dtype or q.dtype, device=dev)
         ys = ctypes.byref(_seq(y)[0])
     pc, keep = (prologue.to_c(D, dev) if prologue is not None else (None, None))
-    rc = L_.pma_selective_prefill(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs),
-                                  ctypes.byref(pc) if pc is not None else None, ld.data_ptr(), bt.data_ptr(),
-                                  st_in, st_out, float(eps), ys, _stream(dev))
+    pref = ctypes.byref(pc) if pc is not None else None
+    ws_bytes = L_.pma_selective_prefill_workspace_bytes(B, H, L, D, _DT[q.dtype], pref)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    rc = L_.pma_selective_prefill(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), pref,
+                                  ld.data_ptr(), bt.data_ptr(), st_in, st_out, float(eps), ys,
+                                  ws.data_ptr() if ws is not None else None, ws_bytes, _stream(dev))
     _lib.check("pma_selective_prefill", rc)
     return y, st_out_t
 

@@ -54,12 +54,12 @@ def test_selective_step_golden(via):
     _check_state(st, [g["st_" + n] for n in NAMES], TOL_F32)
 
 
-def _case(B, H, L, D, seed, dtype):
+def _case(B, H, L, D, seed, dtype, tau_range=(3.0, 2000.0)):
     gen = torch.Generator().manual_seed(seed)
     q = F.normalize(torch.randn(B, H, L, D, generator=gen), dim=-1) / D ** 0.5
     k = F.normalize(torch.randn(B, H, L, D, generator=gen), dim=-1)
     v = torch.randn(B, H, L, D, generator=gen)
-    tau = torch.exp(torch.empty(H).uniform_(np.log(3.0), np.log(2000.0), generator=gen))
+    tau = torch.exp(torch.linspace(np.log(tau_range[0]), np.log(tau_range[1]), H))
     delta = F.softplus(torch.randn(B, L, H, generator=gen)).clamp(1e-4, 50.0)
     ld = (-delta / tau.view(1, 1, H)).transpose(1, 2).contiguous()
     beta = torch.exp(torch.randn(H, generator=gen) * 0.4).clamp(0.1, 15.0)
@@ -73,15 +73,19 @@ def _state(B, H, D, seed):
     return tuple(s)
 
 
-@pytest.mark.parametrize("B,H,L,D,dtype,with_state", [
-    (2, 3, 200, 64, torch.float32, False), (1, 2, 130, 128, torch.float32, True),
-    (2, 2, 77, 32, torch.float32, True), (2, 4, 300, 64, torch.bfloat16, True),
-    (1, 2, 1, 16, torch.bfloat16, True), (1, 3, 1000, 64, torch.bfloat16, False),
+@pytest.mark.parametrize("B,H,L,D,dtype,with_state,taus", [
+    (2, 3, 200, 64, torch.float32, False, (3.0, 2000.0)), (1, 2, 130, 128, torch.float32, True, (3.0, 2000.0)),
+    (2, 2, 77, 32, torch.float32, True, (3.0, 2000.0)),
+    (2, 4, 300, 64, torch.bfloat16, True, (3.0, 2000.0)),     # tensor cores
+    (1, 2, 1, 16, torch.bfloat16, True, (3.0, 2000.0)),
+    (1, 3, 1000, 64, torch.bfloat16, False, (3.0, 2000.0)),   # tensor cores, 8 chunks, ragged tail
+    (2, 4, 260, 64, torch.bfloat16, True, (0.3, 30.0)),       # steep heads fall back to CUDA cores
+    (1, 2, 128, 64, torch.bfloat16, False, (1.2, 1.5)),       # chunk decay near the e^-76 edge
 ])
-def test_selective_prefill_vs_oracle(B, H, L, D, dtype, with_state):
+def test_selective_prefill_vs_oracle(B, H, L, D, dtype, with_state, taus):
     from prime_moment_attention_b200 import ops
     tol = TOL_F32 if dtype == torch.float32 else TOL_BF16
-    q, k, v, ld, beta = _case(B, H, L, D, seed=L + D, dtype=dtype)
+    q, k, v, ld, beta = _case(B, H, L, D, seed=L + D, dtype=dtype, tau_range=taus)
     st = _state(B, H, D, seed=3) if with_state else None
     y, s = ops.selective_prefill(q.cuda(), k.cuda(), v.cuda(), ld.cuda(), beta.cuda(),
                                  state=None if st is None else tuple(t.cuda() for t in st), out_dtype=torch.float32)
@@ -136,12 +140,13 @@ def _module_reference(m, x, state, exact):
 
 
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, TOL_F32), (torch.bfloat16, TOL_BF16)])
-@pytest.mark.parametrize("L,with_state", [(1, True), (150, False), (150, True)])
-def test_selective_module_forward(dtype, tol, L, with_state):
+@pytest.mark.parametrize("L,with_state,D", [(1, True, 32), (150, False, 32), (150, True, 32), (300, True, 64)])
+def test_selective_module_forward(dtype, tol, L, with_state, D):
+    """D = 64 bf16 runs the tensor-core path with the QK-norm pass in front of it."""
     import prime_moment_attention_b200 as pma
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.manual_seed(0)
-    m = pma.PrimeSelectiveMomentAttention(hidden_size=128, num_heads=4, head_dim=32, num_kv_heads=2, decay=0.99)
+    m = pma.PrimeSelectiveMomentAttention(hidden_size=128, num_heads=4, head_dim=D, num_kv_heads=2, decay=0.99)
     with torch.no_grad():
         m.delta_proj.weight.normal_(0, 0.1)
         m.log_tau.copy_(torch.log(torch.tensor([3.0, 30.0, 300.0, 1500.0])))
@@ -151,7 +156,7 @@ def test_selective_module_forward(dtype, tol, L, with_state):
             ln.bias.uniform_(-0.1, 0.1)
     m = m.to("cuda", dtype)
     x = torch.randn(2, L, 128, generator=torch.Generator().manual_seed(1)).to("cuda", dtype)
-    st = tuple(t.cuda() for t in _state(2, 4, 32, seed=5)) if with_state else None
+    st = tuple(t.cuda() for t in _state(2, 4, D, seed=5)) if with_state else None
     with torch.inference_mode():
         out, s = m(x, state=st, return_state=True)
         torch.cuda.synchronize()
