@@ -511,7 +511,9 @@ int pma_delta_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const
     p.norm_eps = norm_eps;
     p.state_in = state_in;
     p.state_out = state_out;
-    cudaError_t e = launch_delta_prefill(p, D, chunk, q->dtype, y ? y->dtype : PMA_F32, st);
+    cudaError_t e = delta_tc_supported(D, chunk, q->dtype)
+                        ? launch_delta_prefill_tc(p, y ? y->dtype : PMA_F32, st)
+                        : launch_delta_prefill(p, D, chunk, q->dtype, y ? y->dtype : PMA_F32, st);
     return e == cudaSuccess ? PMA_OK : cuda_fail(e);
 }
 

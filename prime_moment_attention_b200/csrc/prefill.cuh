@@ -69,6 +69,8 @@ struct DeltaStepParams {
     float *state_out;
 };
 bool delta_supported(int D, int chunk);
+bool delta_tc_supported(int D, int chunk, int idt);
+cudaError_t launch_delta_prefill_tc(const DeltaParams &p, int ydt, cudaStream_t st);
 cudaError_t launch_delta_prefill(const DeltaParams &p, int D, int chunk, int idt, int ydt, cudaStream_t st);
 cudaError_t launch_delta_step(const DeltaStepParams &p, int D, int idt, int ydt, cudaStream_t st);
 
