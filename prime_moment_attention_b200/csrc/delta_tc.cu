@@ -16,7 +16,9 @@
 //           S *= min(1, bound / (|S|_F + 1e-6)), and its bf16 copy for the next chunk's MMA 1
 //   y       y_i = exp(cum_i) (Psi S^T)_i + y_intra_i
 //
-// Shared memory (about 104 KB): the [Phi ; Psi] operand as two K-halves of 128 x 64 bf16
+// q, k, v rows of the next chunk are copied into padded staging tiles with cp.async while the
+// current chunk computes.
+// Shared memory (about 116 KB): the [Phi ; Psi] operand as two K-halves of 128 x 64 bf16
 // (128-byte swizzle), the bf16 state tile S^T [128 x 64] (MN-major B operand), the bf16 tiles of
 // beta E and coef E [64 x 64] (MN-major B operands), and float32 T, u/E and the block inverses.
 // Tensor memory (256 columns): D1 in 0..127 (P overwrites the psi rows' columns 0..31 once
@@ -49,12 +51,21 @@ constexpr int OFF_TI = OFF_VE + C * VS * 4;          // inverses of T's diagonal
 constexpr int OFF_VEC = OFF_TI + (C / 16) * 256 * 4;  // cum, beta, exp(cum), coef: [4][64]
 constexpr int OFF_RED = OFF_VEC + 4 * C * 4;          // [16] reductions
 constexpr int OFF_BAR = OFF_RED + 16 * 4;             // mbarrier, tmem base, abort flag
-constexpr int SMEM_USED = OFF_BAR + 32;
+constexpr int STG_ROW = 144;                          // staging row: 128 B of bf16 + 16 B pad
+constexpr int OFF_STG = OFF_BAR + 32;                 // next chunk's k, q, v rows (cp.async)
+constexpr int STG_TILE = C * STG_ROW;
+constexpr int SMEM_USED = OFF_STG + 3 * STG_TILE;
 constexpr size_t SMEM_BYTES = SMEM_USED + 1024;      // + alignment of the swizzled tiles
 constexpr uint32_t T_D1 = 0, T_Y = 128, T_DS = 192, T_COLS = 256;
 
 // 16-byte chunk c of row r in a [rows x 128 B] 128-byte-swizzled tile
 __device__ __forceinline__ uint32_t sw(int r, int c) { return swz(r, c); }
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
@@ -130,74 +141,82 @@ __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
     const uint32_t a0 = sb >> 4;
     auto dsc = [&](uint32_t off, uint64_t hi) { return (uint64_t)(a0 + (off >> 4)) | hi; };
 
+    // rows of chunk t0 into the staging tiles (k, q, v; 16-byte asynchronous copies)
+    auto stage = [&](int t0) {
+        const int nn = min(C, p.L - t0);
+        for (int e = tid; e < 3 * C * 8; e += NT) {
+            const int which = e / (C * 8), rem = e - which * (C * 8), row = rem >> 3, c = rem & 7;
+            if (row >= nn || (which == 1 && !want_y)) continue;
+            const TI *src = which == 0 ? kb + (int64_t)(t0 + row) * p.k.sl
+                                       : (which == 1 ? qb + (int64_t)(t0 + row) * p.q.sl : vb + (int64_t)(t0 + row) * p.v.sl);
+            cp_async16(smem + OFF_STG + which * STG_TILE + row * STG_ROW + 16 * c, src + 8 * c);
+        }
+        cp_async_commit();
+    };
+    if (p.L > 0) stage(0);
+    // warp 7: the gates of tokens 2 lane, 2 lane + 1 of the next chunk, loaded a chunk ahead
+    float gb[2] = {0.f, 0.f}, ga[2] = {lam, lam};
+    auto load_gates = [&](int t0) {
+        const int nn = min(C, p.L - t0);
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            const int i = lane * 2 + m;
+            gb[m] = i < nn ? beta_g[t0 + i] : 0.f;
+            ga[m] = (i < nn && alpha_g) ? alpha_g[t0 + i] : lam;
+        }
+    };
+    if (warp == 7 && p.L > 0) load_gates(0);
+
     bool ok = true;
     for (int t0 = 0; t0 < p.L && ok; t0 += C) {
         const int n = min(C, p.L - t0);
-        // ---- A. features into the operand tiles (bf16), v rows, gates
-        if (tid < 2 * C) {
-            const bool is_q = tid >= C;
-            const int i = tid & (C - 1);
-            const TI *src = is_q ? qb + (int64_t)(t0 + i) * p.q.sl : kb + (int64_t)(t0 + i) * p.k.sl;
-            float x[D];
+        cp_async_wait_all();
+        __syncthreads();
+        // ---- A. features into the operand tiles (bf16): two threads per row (lanes 2r, 2r + 1 of
+        // warp w hold row 16 w + r: k rows 0..63 in warps 0-3, q rows in warps 4-7), 32 elements each
+        {
+            const int row = tid >> 1, hf = tid & 1;
+            const bool is_q = row >= C;
+            const int i = row & (C - 1);
+            const uint8_t *srow = smem + OFF_STG + (is_q ? STG_TILE : 0) + i * STG_ROW + 64 * hf;
+            float x[32];
             if (i < n) {
 #pragma unroll
-                for (int d = 0; d < D; d += 4) {
-                    const float4 v4 = load4(src + d);
-                    x[d] = v4.x; x[d + 1] = v4.y; x[d + 2] = v4.z; x[d + 3] = v4.w;
+                for (int c = 0; c < 4; ++c) {
+                    const uint4 u4 = *reinterpret_cast<const uint4 *>(srow + 16 * c);
+                    const float2 a = bf2f(u4.x), bq = bf2f(u4.y), cq = bf2f(u4.z), dq = bf2f(u4.w);
+                    x[8 * c] = a.x; x[8 * c + 1] = a.y; x[8 * c + 2] = bq.x; x[8 * c + 3] = bq.y;
+                    x[8 * c + 4] = cq.x; x[8 * c + 5] = cq.y; x[8 * c + 6] = dq.x; x[8 * c + 7] = dq.y;
                 }
             } else {
 #pragma unroll
-                for (int d = 0; d < D; ++d) x[d] = 0.f;
+                for (int d = 0; d < 32; ++d) x[d] = 0.f;
             }
             float s1 = 1.f, s2 = r2;
-            if (!is_q) {
+            if (!is_q) {  // warp-uniform: warps 0-3 hold k rows
                 float n1 = 0.f, n2 = 0.f;
 #pragma unroll
-                for (int d = 0; d < D; ++d) {
+                for (int d = 0; d < 32; ++d) {
                     const float k2 = x[d] * x[d];
                     n1 = fmaf(x[d], x[d], n1);
                     n2 = fmaf(k2, k2, n2);
                 }
+                n1 += __shfl_xor_sync(0xffffffffu, n1, 1);
+                n2 += __shfl_xor_sync(0xffffffffu, n2, 1);
                 s1 = 1.0f / fmaxf(sqrtf(n1), p.norm_eps);
                 s2 = r2 / fmaxf(sqrtf(n2), p.norm_eps);
             }
             if (is_q && !want_y) s1 = s2 = 0.f;
-            const int row = is_q ? C + i : i;
             float t[8];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
+            for (int c = 0; c < 4; ++c) {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) t[e] = x[8 * c + e] * s1;
-                *reinterpret_cast<uint4 *>(smem + OFF_A + sw(row, c)) = pack8(t);
+                *reinterpret_cast<uint4 *>(smem + OFF_A + sw(row, 4 * hf + c)) = pack8(t);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) t[e] = x[8 * c + e] * x[8 * c + e] * s2;
-                *reinterpret_cast<uint4 *>(smem + OFF_AH + sw(row, c)) = pack8(t);
+                *reinterpret_cast<uint4 *>(smem + OFF_AH + sw(row, 4 * hf + c)) = pack8(t);
             }
-        } else if (tid < 2 * C + C) {
-            const int j = tid - 2 * C;
-            float4 *dst = reinterpret_cast<float4 *>(VE + j * VS);
-#pragma unroll
-            for (int d = 0; d < D; d += 4) dst[d / 4] = j < n ? load4(vb + (int64_t)(t0 + j) * p.v.sl + d) : make_float4(0, 0, 0, 0);
-        } else if (warp == 7) {  // gates and the inclusive scan of log alpha (2 tokens per lane)
-            float la[2], run = 0.f;
-#pragma unroll
-            for (int m = 0; m < 2; ++m) {
-                const int i = lane * 2 + m;
-                float a = lam_c;
-                if (i < n) a = fminf(fmaxf(alpha_g ? alpha_g[t0 + i] : lam, 1e-5f), 1.0f);
-                run += __logf(a);
-                la[m] = run;
-                bet[i] = i < n ? beta_g[t0 + i] : 0.f;
-            }
-            float incl = run;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const float tt = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += tt;
-            }
-            const float base = incl - run;
-            cum[lane * 2] = base + la[0];
-            cum[lane * 2 + 1] = base + la[1];
         }
         fence_proxy_async();
         tc_fence_before();
@@ -217,51 +236,88 @@ __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
                        dsc(OFF_ST, HI_MN1) + (uint64_t)(k * 128), ID_1S, k > 0);
             commit(bar);
         }
-        if (tid < C) {  // exp(cum) and the state-update weights while the MMAs run
-            const float ce = cum[C - 1];
-            din[tid] = __expf(cum[tid]);
-            coef[tid] = bet[tid] * __expf(ce - cum[tid]);
+        // while the MMAs run: v rows into u's buffer (warps 4-5), the gates' scan, exp(cum) and the
+        // state-update weights (warp 7)
+        if (warp == 4 || warp == 5) {
+            const int j = tid - 128;
+            float4 *dst = reinterpret_cast<float4 *>(VE + j * VS);
+            const uint8_t *srow = smem + OFF_STG + 2 * STG_TILE + j * STG_ROW;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                float4 lo = make_float4(0, 0, 0, 0), hi = lo;
+                if (j < n) {
+                    const uint4 u4 = *reinterpret_cast<const uint4 *>(srow + 16 * c);
+                    const float2 a = bf2f(u4.x), bq = bf2f(u4.y), cq = bf2f(u4.z), dq = bf2f(u4.w);
+                    lo = make_float4(a.x, a.y, bq.x, bq.y);
+                    hi = make_float4(cq.x, cq.y, dq.x, dq.y);
+                }
+                dst[2 * c] = lo;
+                dst[2 * c + 1] = hi;
+            }
+        } else if (warp == 7) {  // inclusive scan of log alpha (2 tokens per lane)
+            float la[2], run = 0.f;
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const int i = lane * 2 + m;
+                const float a = i < n ? fminf(fmaxf(ga[m], 1e-5f), 1.0f) : lam_c;
+                run += __logf(a);
+                la[m] = run;
+                bet[i] = i < n ? gb[m] : 0.f;
+            }
+            float incl = run;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float tt = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += tt;
+            }
+            const float base = incl - run;
+            la[0] += base;
+            la[1] += base;
+            const float ce = __shfl_sync(0xffffffffu, la[1], 31);
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const int i = lane * 2 + m;
+                cum[i] = la[m];
+                din[i] = __expf(la[m]);
+                coef[i] = bet[i] * __expf(ce - la[m]);
+            }
         }
+        if (warp == 7 && t0 + C < p.L) load_gates(t0 + C);  // this chunk's gates are consumed
         bool w_ok = mbar_wait(bar, mma_phase, ctl, 1);
         mma_phase ^= 1;
         if (!__syncthreads_and(w_ok)) { ok = false; break; }
         tc_fence_after();
-        // ---- C. T and u (phi rows, warps 0-1), P in bf16 (psi rows, warps 2-3)
-        if (warp < 2) {
-            const int i = tid;  // tensor-memory lane = phi row i
-            const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16);
+        // the staging tiles are consumed (features in phase A, v rows in phase B): the next chunk's
+        // rows land while this one computes
+        if (t0 + C < p.L) stage(t0 + C);
+        // ---- C. T and u (phi rows: warps 0, 1, 4, 5), P in bf16 (psi rows: warps 2, 3, 6, 7); warps w and
+        // w + 4 share a tensor-memory lane quadrant and take one half of its columns each
+        {
+            const int quad = warp & 3, hc = warp >> 2;  // column half
+            const uint32_t lb = tmem + ((uint32_t)(quad * 32) << 16);
             float g[32];
-            const float ci = cum[i];
-#pragma unroll
-            for (int hc = 0; hc < 2; ++hc) {
+            if (quad < 2) {
+                const int i = quad * 32 + lane;  // phi row i
+                const float ci = cum[i];
                 tmem_ld32(lb + T_D1 + 32 * hc, g);
 #pragma unroll
                 for (int e = 0; e < 32; ++e) {
                     const int j = 32 * hc + e;
-                    const float tv = j < i ? __expf(ci - cum[j]) * g[e] * bet[j] : (j == i ? 1.f : 0.f);
-                    Tt[j * C + i] = tv;
+                    Tt[j * C + i] = j < i ? __expf(ci - cum[j]) * g[e] * bet[j] : (j == i ? 1.f : 0.f);
                 }
-            }
-            const float di = din[i];
-            float4 *ve = reinterpret_cast<float4 *>(VE + i * VS);
-#pragma unroll
-            for (int hc = 0; hc < 2; ++hc) {
+                const float di = din[i];
+                float4 *ve = reinterpret_cast<float4 *>(VE + i * VS + 32 * hc);
                 tmem_ld32(lb + T_D1 + 64 + 32 * hc, g);
 #pragma unroll
                 for (int e = 0; e < 32; e += 4) {
-                    float4 v4 = ve[(32 * hc + e) / 4];
+                    float4 v4 = ve[e / 4];
                     v4.x -= di * g[e]; v4.y -= di * g[e + 1]; v4.z -= di * g[e + 2]; v4.w -= di * g[e + 3];
-                    ve[(32 * hc + e) / 4] = v4;
+                    ve[e / 4] = v4;
                 }
-            }
-        } else if (warp < 4) {
-            const int i = tid - 64;  // tensor-memory lane 64 + i = psi row i
-            const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16);
-            const float ci = cum[i];
-            float g[32];
-            uint32_t pk[16];
-#pragma unroll
-            for (int hc = 0; hc < 2; ++hc) {
+            } else {
+                const int i = (quad - 2) * 32 + lane;  // psi row i (tensor-memory lane 64 + i)
+                const float ci = cum[i];
+                uint32_t pk[16];
                 tmem_ld32(lb + T_D1 + 32 * hc, g);
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
@@ -270,29 +326,38 @@ __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
                     const float p1 = j + 1 <= i ? __expf(ci - cum[j + 1]) * g[e + 1] : 0.f;
                     pk[e / 2] = pack2(p0, p1);
                 }
-                tmem_st16(lb + T_D1 + 16 * hc, pk);  // P row i, bf16 pairs, columns 0..31
+                // P row i as bf16 pairs goes to columns 16 hc .. 16 hc + 15; columns 16..31 are still
+                // scores that the hc = 0 warp of this quadrant reads, so the four psi warps write only
+                // after all of them have their scores in registers
+                tc_fence_before();
+                named_bar(2, 128);
+                tc_fence_after();
+                tmem_st16(lb + T_D1 + 16 * hc, pk);
+                tmem_wait_st();
             }
-            tmem_wait_st();
         }
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
         // ---- D. solve T E = u: inverses of the diagonal blocks, then block substitution
-        if (tid < C) {
-            const int bi = tid >> 4, c = tid & 15, r0 = bi * 16;
+        {  // inverses of the diagonal blocks: thread (block, column c, k-quarter kq); the four threads
+           // of a column split each row's sum over k and join it with two shuffles
+            const int bi = tid >> 6, c = (tid >> 2) & 15, kq = tid & 3, r0 = bi * 16;
             float x[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-                float s = (i == c) ? 1.f : 0.f;
-                if (i > c) {
+                float s = 0.f;
 #pragma unroll
-                    for (int k = 0; k < 16; ++k)
-                        if (k >= c && k < i) s = fmaf(-Tt[(r0 + k) * C + r0 + i], x[k], s);
-                }
-                x[i] = s;
+                for (int k = 0; k < 16; ++k)
+                    if ((k & 3) == kq && k >= c && k < i) s = fmaf(-Tt[(r0 + k) * C + r0 + i], x[k], s);
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                s += __shfl_xor_sync(0xffffffffu, s, 2);
+                x[i] = i == c ? 1.f : (i > c ? s : 0.f);
             }
+            if (kq == 0) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) TIv[(bi * 16 + i) * 16 + c] = x[i];
+                for (int i = 0; i < 16; ++i) TIv[(bi * 16 + i) * 16 + c] = x[i];
+            }
         }
         __syncthreads();
         {
@@ -410,6 +475,7 @@ __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
         tc_fence_after();
     }
 
+    cp_async_wait_all();  // no copy may still target this CTA's shared memory at exit
     // ---- state out (S^T row f -> S[d][f])
     if (ok && st_thr && p.state_out) {
         float *so = p.state_out + (size_t)bh * D * F;
