@@ -281,11 +281,20 @@ __global__ void __launch_bounds__(DT, 1) delta_prefill_kernel(const DeltaParams 
                 const int r = bi * 16 + rl;
                 if (act && bi > 0) {
                     float4 acc = *reinterpret_cast<const float4 *>(VE + r * D + dd);
-                    for (int j = 0; j < bi * 16; ++j) {
-                        const float tj = Tt[j * C + r];
-                        const float4 ej = *reinterpret_cast<const float4 *>(VE + j * D + dd);
-                        acc.x = fmaf(-tj, ej.x, acc.x); acc.y = fmaf(-tj, ej.y, acc.y);
-                        acc.z = fmaf(-tj, ej.z, acc.z); acc.w = fmaf(-tj, ej.w, acc.w);
+                    for (int jb = 0; jb < bi; ++jb) {  // 16 rows per pass, unrolled: the loads pipeline
+                        float4 a2 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj += 2) {
+                            const int j = jb * 16 + jj;
+                            const float t0v = Tt[j * C + r], t1v = Tt[(j + 1) * C + r];
+                            const float4 e0 = *reinterpret_cast<const float4 *>(VE + j * D + dd);
+                            const float4 e1 = *reinterpret_cast<const float4 *>(VE + (j + 1) * D + dd);
+                            acc.x = fmaf(-t0v, e0.x, acc.x); acc.y = fmaf(-t0v, e0.y, acc.y);
+                            acc.z = fmaf(-t0v, e0.z, acc.z); acc.w = fmaf(-t0v, e0.w, acc.w);
+                            a2.x = fmaf(-t1v, e1.x, a2.x); a2.y = fmaf(-t1v, e1.y, a2.y);
+                            a2.z = fmaf(-t1v, e1.z, a2.z); a2.w = fmaf(-t1v, e1.w, a2.w);
+                        }
+                        acc.x += a2.x; acc.y += a2.y; acc.z += a2.z; acc.w += a2.w;
                     }
                     *reinterpret_cast<float4 *>(VE + r * D + dd) = acc;
                 }
@@ -303,8 +312,8 @@ __global__ void __launch_bounds__(DT, 1) delta_prefill_kernel(const DeltaParams 
                 }
                 __syncthreads();
                 if (act) *reinterpret_cast<float4 *>(VE + r * D + dd) = e4;
+                __syncthreads();  // the next block's R step reads these E rows
             }
-            __syncthreads();
         }
         // ---- E1. y = y_inter + P (beta E) on this thread's B2 tile ----
         if (t2 && want_y) {

@@ -367,11 +367,20 @@ __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
                 const int r = bi * 16 + rl;
                 if (bi > 0) {
                     float4 acc = *reinterpret_cast<const float4 *>(VE + r * VS + dd);
-                    for (int j = 0; j < bi * 16; ++j) {
-                        const float tj = Tt[j * C + r];
-                        const float4 ej = *reinterpret_cast<const float4 *>(VE + j * VS + dd);
-                        acc.x = fmaf(-tj, ej.x, acc.x); acc.y = fmaf(-tj, ej.y, acc.y);
-                        acc.z = fmaf(-tj, ej.z, acc.z); acc.w = fmaf(-tj, ej.w, acc.w);
+                    for (int jb = 0; jb < bi; ++jb) {  // 16 rows per pass, unrolled: the loads pipeline
+                        float4 a2 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj += 2) {
+                            const int j = jb * 16 + jj;
+                            const float t0v = Tt[j * C + r], t1v = Tt[(j + 1) * C + r];
+                            const float4 e0 = *reinterpret_cast<const float4 *>(VE + j * VS + dd);
+                            const float4 e1 = *reinterpret_cast<const float4 *>(VE + (j + 1) * VS + dd);
+                            acc.x = fmaf(-t0v, e0.x, acc.x); acc.y = fmaf(-t0v, e0.y, acc.y);
+                            acc.z = fmaf(-t0v, e0.z, acc.z); acc.w = fmaf(-t0v, e0.w, acc.w);
+                            a2.x = fmaf(-t1v, e1.x, a2.x); a2.y = fmaf(-t1v, e1.y, a2.y);
+                            a2.z = fmaf(-t1v, e1.z, a2.z); a2.w = fmaf(-t1v, e1.w, a2.w);
+                        }
+                        acc.x += a2.x; acc.y += a2.y; acc.z += a2.z; acc.w += a2.w;
                     }
                     *reinterpret_cast<float4 *>(VE + r * VS + dd) = acc;
                 }
@@ -387,8 +396,8 @@ __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
                 }
                 __syncthreads();
                 *reinterpret_cast<float4 *>(VE + r * VS + dd) = e4;
+                __syncthreads();  // the next block's R step reads these E rows
             }
-            __syncthreads();
         }
         // beta E and coef E as bf16 MN-major tiles (row j = token, 64 value columns)
         if (tid < 2 * C) {
