@@ -396,13 +396,18 @@ def bench_delta(args, ws, rank, device, stream, peaks):
     tf = tokheads * DELTA_FLOP_PER_TOKHEAD / (ms * 1e-3) / 1e12
     bw = tokheads * DELTA_BYTES_PER_TOKHEAD / (ms * 1e-3) / 1e9
     pre = {"metric": "delta_prefill_tok_per_s", "value": round(B * L * ws / (ms * 1e-3), 1), "unit": "tok/s",
-           "ms_per_step": round(ms, 4), "steps": steps, "higher_is_better": True, "dtype": "bf16 in, fp32 math",
-           "config": {"workload": "config2 delta-rule prefill: B=8 seqs/GPU, H=12, D=64, L=8192, chunk 64, bf16 "
+           "ms_per_step": round(ms, 4), "steps": steps, "higher_is_better": True, "dtype": "bf16 products, f32 solve and state",
+           "config": {"workload": "config2 delta-rule prefill on tensor cores: B=8 seqs/GPU, H=12, D=64, L=8192, "
+                                  "chunk 64, bf16 "
                                   "q/k/v, beta_t=sigmoid(N(0,1)), alpha_t=lambda_h, Lyapunov bound 25"},
-           "roofline": {"bound": "fp32 CUDA cores", "achieved": round(tf, 2), "peak": round(FP32_SIMT_PEAK_TFLOPS, 1),
-                        "unit": "TFLOP/s", "frac": round(tf / FP32_SIMT_PEAK_TFLOPS, 4), "traffic": None,
-                        "peak_kind": "nominal (148 SMs x 128 FMA/clk x 1965 MHz); one CTA per head-state, "
-                                     f"{min(B * H, 148)} of 148 SMs busy",
+           "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": peaks[1], "unit": "TFLOP/s",
+                        "frac": round(tf / peaks[1], 4), "traffic": None, "peak_kind": peak_kind,
+                        "note": "latency of the sequential chunk recurrence: one CTA per head-state "
+                                f"({min(B * H, 148)} of 148 SMs busy); the float32 triangular solve on the CUDA "
+                                "cores is the longest phase of a chunk",
+                        "fp32_cuda_cores": {"achieved": round(tf, 2), "peak": round(FP32_SIMT_PEAK_TFLOPS, 1),
+                                            "frac": round(tf / FP32_SIMT_PEAK_TFLOPS, 4),
+                                            "peak_kind": "nominal (148 SMs x 128 FMA/clk x 1965 MHz)"},
                         "hbm": {"achieved": round(bw, 1), "peak": hbm_peak, "unit": "GB/s",
                                 "frac": round(bw / hbm_peak, 4), "peak_kind": peak_kind},
                         "algorithmic_flop_per_launch": tokheads * DELTA_FLOP_PER_TOKHEAD},
