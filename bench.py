@@ -538,16 +538,17 @@ def bench_sp(args, ws, rank, device, stream, peaks):
     bw = tokheads * SP_BYTES_PER_TOKHEAD / (ms * 1e-3) / 1e9
     return {"metric": "sp_prefill_tok_per_s", "value": round(c["B"] * c["L"] / (ms * 1e-3), 1), "unit": "tok/s",
             "ms_per_step": round(ms, 3), "steps": steps, "higher_is_better": True, "scaling": "strong",
-            "dtype": "bf16 in, fp32 math",
+            "dtype": "bf16",
             "config": {"workload": "config5 long-sequence prefill: B=1, H=16, D=128, L=2^20 bf16, per-head lambda "
                                    f"log-U[0.999,0.99995], {ws} contiguous shard(s) of {Ls} tokens",
-                       "path": "pma_prefill (CUDA cores at D=128, segments across CTAs)" if ws == 1 else
+                       "path": "pma_prefill (tensor cores at D=128, segments across CTAs)" if ws == 1 else
                                "sequence_parallel_prefill: state-only pass, NCCL all_gather, prefix fold, full pass"},
-            "roofline": {"bound": "fp32 CUDA cores", "achieved": round(tf, 2), "peak": round(FP32_SIMT_PEAK_TFLOPS, 1),
-                         "unit": "TFLOP/s", "frac": round(tf / FP32_SIMT_PEAK_TFLOPS, 4), "traffic": None,
-                         "peak_kind": "nominal (148 SMs x 128 FMA/clk x 1965 MHz) per GPU x " + str(ws),
-                         "hbm": {"achieved": round(bw, 1), "peak": hbm_peak * ws, "unit": "GB/s",
-                                 "frac": round(bw / (hbm_peak * ws), 4), "peak_kind": peak_kind},
+            "roofline": {"bound": "hbm", "achieved": round(bw, 1), "peak": hbm_peak * ws, "unit": "GB/s",
+                         "frac": round(bw / (hbm_peak * ws), 4), "traffic": None,
+                         "peak_kind": f"{peak_kind} per GPU x {ws}",
+                         "tensor": {"achieved": round(tf, 2), "peak": round(peaks[1] * ws, 1), "unit": "TFLOP/s",
+                                    "frac": round(tf / (peaks[1] * ws), 4)},
+                         "algorithmic_bytes_per_step": tokheads * SP_BYTES_PER_TOKHEAD,
                          "algorithmic_flop_per_step": tokheads * SP_FLOP_PER_TOKHEAD},
             "gpu_launches": None, "clocks": clk_r}
 

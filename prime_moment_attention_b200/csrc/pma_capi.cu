@@ -100,9 +100,21 @@ struct Plan {
     size_t ws_bytes = 0;
 };
 
-Plan make_plan(int B, int H, int L, int D, int dtype, int sms) {
+bool bf16_exact(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return (u & 0xffffu) == 0;
+}
+
+// D = 128 runs on tensor cores when the kernel needs no LayerNorm pass (`pro` null: no prologue).
+bool tc128_plan(int D, int dtype, const Prologue *pro) {
+    if (D != 128 || !tc128_supported(dtype)) return false;
+    return !pro || (!pro->qw && !pro->kw && (pro->q_scale == 1.0f || bf16_exact(pro->q_scale)));
+}
+
+Plan make_plan(int B, int H, int L, int D, int dtype, int sms, const Prologue *pro) {
     Plan p;
-    p.tc = tc_supported(D, dtype);
+    p.tc = tc_supported(D, dtype) || tc128_plan(D, dtype, pro);
     p.chunk = p.tc ? TC_CHUNK : simt_chunk(D);
     const long BH = (long)B * H;
     const int nchunks = (L + p.chunk - 1) / p.chunk;
@@ -152,12 +164,6 @@ int decode_impl(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tens
                 int pool_rows, const pma_state *state_in, const pma_state *state_out, float eps,
                 const pma_seq_tensor *y, pma_stream_t stream, const float *k_head_scale = nullptr,
                 bool selective = false);
-
-bool bf16_exact(float f) {
-    uint32_t u;
-    memcpy(&u, &f, 4);
-    return (u & 0xffffu) == 0;
-}
 
 // Tensor-core path: which inputs the QK-norm pass rewrites, and the workspace beyond the plan's.
 struct ProPass {
@@ -224,7 +230,8 @@ Plan selective_plan(int L, int D, int dtype) {
 
 cudaError_t launch_prefill(const Plan &pl, const PrefillParams &p, int D, int idt, int ydt, dim3 grid,
                            cudaStream_t st) {
-    return pl.tc ? launch_prefill_tc(p, ydt, grid, st) : launch_prefill_simt(p, D, idt, ydt, grid, st);
+    if (!pl.tc) return launch_prefill_simt(p, D, idt, ydt, grid, st);
+    return D == 128 ? launch_prefill_tc128(p, ydt, grid, st) : launch_prefill_tc(p, ydt, grid, st);
 }
 
 }  // namespace
@@ -265,7 +272,7 @@ size_t pma_prefill_workspace_bytes(int B, int H, int L, int D, int dtype) {
     if (B <= 0 || H <= 0 || L <= 0 || !supported_d(D) || !supported_dtype(dtype)) return 0;
     DevInfo di;
     if (device_info(&di) != PMA_OK) return 0;
-    return make_plan(B, H, L, D, dtype, di.sms).ws_bytes;
+    return make_plan(B, H, L, D, dtype, di.sms, nullptr).ws_bytes;
 }
 
 size_t pma_prefill_ex_workspace_bytes(int B, int H, int L, int D, int dtype, const pma_prologue *prologue) {
@@ -274,7 +281,7 @@ size_t pma_prefill_ex_workspace_bytes(int B, int H, int L, int D, int dtype, con
     if (prologue_of(prologue, H, &pro) != PMA_OK) return 0;
     DevInfo di;
     if (device_info(&di) != PMA_OK) return 0;
-    return pro_pass(make_plan(B, H, L, D, dtype, di.sms), pro, B, H, L, true).total;
+    return pro_pass(make_plan(B, H, L, D, dtype, di.sms, &pro), pro, B, H, L, true).total;
 }
 
 int pma_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
@@ -361,7 +368,7 @@ int prefill_impl(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_
         return PMA_OK;
     }
 
-    const Plan pl = make_plan(B, H, L, D, q->dtype, di.sms);
+    const Plan pl = make_plan(B, H, L, D, q->dtype, di.sms, &pro);
     const ProPass pp = pro_pass(pl, pro, B, H, L, y != nullptr);
     if (pp.total && (!workspace || workspace_bytes < pp.total)) return PMA_ERR_WORKSPACE;
     if (pp.total && reinterpret_cast<uintptr_t>(workspace) % 16) return PMA_ERR_WORKSPACE;

@@ -91,5 +91,9 @@ cudaError_t launch_qk_norm(const Seq &src, int B, int Hs, int L, const float *w,
 constexpr int TC_CHUNK = 128;
 bool tc_supported(int D, int idt);
 cudaError_t launch_prefill_tc(const PrefillParams &p, int ydt, dim3 grid, cudaStream_t st);
+// tcgen05 tensor-core prefill for D = 128 (bf16 inputs, per-head decay, no LayerNorm prologue,
+// q scale exact in bf16).
+bool tc128_supported(int idt);
+cudaError_t launch_prefill_tc128(const PrefillParams &p, int ydt, dim3 grid, cudaStream_t st);
 
 }  // namespace pma

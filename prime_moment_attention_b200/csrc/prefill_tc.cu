@@ -836,16 +836,19 @@ static EncodeTiled get_encode() {
     return fn;
 }
 
-// [B,H,L,64] bf16 with element strides -> 4-D map (d, l, h, b), box 64 x 128 x 1 x 1, 128-byte swizzle.
-static bool make_map(CUtensorMap *m, const Seq &s, int B, int H, int L) {
+bool tensor_maps_available() { return get_encode() != nullptr; }
+
+// [B,H,L,Dh] bf16 with element strides -> 4-D map (d, l, h, b), box 64 x 128 x 1 x 1, 128-byte
+// swizzle (Dh = 128: two boxes per row block, at d = 0 and d = 64).
+bool make_tile_map(CUtensorMap *m, const Seq &s, int B, int H, int L, int Dh) {
     EncodeTiled enc = get_encode();
     if (!enc) return false;
-    const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)L, (cuuint64_t)H, (cuuint64_t)B};
+    const cuuint64_t dims[4] = {(cuuint64_t)Dh, (cuuint64_t)L, (cuuint64_t)H, (cuuint64_t)B};
     // strides of dims 1..3 in bytes; size-1 dims get a harmless stride
     cuuint64_t str[3] = {(cuuint64_t)s.sl * 2, (cuuint64_t)s.sh * 2, (cuuint64_t)s.sb * 2};
     for (int i = 0; i < 3; ++i)
         if (str[i] == 0) str[i] = 16;
-    const cuuint32_t box[4] = {(cuuint32_t)D, (cuuint32_t)C, 1, 1};
+    const cuuint32_t box[4] = {64, (cuuint32_t)C, 1, 1};
     const cuuint32_t es[4] = {1, 1, 1, 1};
     return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(s.p), dims, str, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -869,9 +872,9 @@ bool tc_supported(int D, int idt) { return D == 64 && idt == PMA_BF16 && tc::get
 cudaError_t launch_prefill_tc(const PrefillParams &p, int ydt, dim3 grid, cudaStream_t st) {
     CUtensorMap mq, mk, mv;
     const int hkv = p.H / p.pro.groups;
-    if (!tc::make_map(&mk, p.k, p.B, hkv, p.L) || !tc::make_map(&mv, p.v, p.B, hkv, p.L)) return cudaErrorInvalidValue;
+    if (!tc::make_tile_map(&mk, p.k, p.B, hkv, p.L, 64) || !tc::make_tile_map(&mv, p.v, p.B, hkv, p.L, 64)) return cudaErrorInvalidValue;
     if (!p.state_only && p.y.p) {
-        if (!tc::make_map(&mq, p.q, p.B, p.H, p.L)) return cudaErrorInvalidValue;
+        if (!tc::make_tile_map(&mq, p.q, p.B, p.H, p.L, 64)) return cudaErrorInvalidValue;
     } else {
         mq = mk;
     }

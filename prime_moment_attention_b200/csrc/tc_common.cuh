@@ -277,5 +277,10 @@ __device__ __forceinline__ uint32_t f2bf(float2 v) { return pack2(v.x, v.y); }
 // byte offset of 16-byte chunk `c` of row `r` in a [rows x 128 B] tile with the 128-byte swizzle
 __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
+// Host side (prefill_tc.cu): the driver's tensor-map encoder is reachable, and a 4-D map
+// (d, l, h, b) over a [B,H,L,Dh] bf16 tensor with a 64 x 128 x 1 x 1 box and the 128-byte swizzle.
+bool tensor_maps_available();
+bool make_tile_map(CUtensorMap *m, const Seq &s, int B, int H, int L, int Dh);
+
 }  // namespace tc
 }  // namespace pma

@@ -1,4 +1,4 @@
-"""Tensor-core (tcgen05) prefill: bf16 inputs, D = 64, against the float64 oracle.
+"""Tensor-core (tcgen05) prefill: bf16 inputs, D = 64 and D = 128, against the float64 oracle.
 
 Bar: 2e-2 max relative error on y and on each final-state component (bf16
 operands, float32 accumulation and state).  Each call also checks the kernel's
@@ -14,8 +14,7 @@ from tests.helpers import TOL_BF16, TOL_F32, assert_close, assert_state_close, c
 pytestmark = pytest.mark.gpu
 
 
-def _run(B, H, L, seed, lam=None, state=None, out_dtype=torch.float32):
-    D = 64
+def _run(B, H, L, seed, lam=None, state=None, out_dtype=torch.float32, D=64):
     q, k, v = synth.make_qkv(B, H, L, D, seed=seed, dtype=torch.bfloat16, device="cuda")
     if lam is None:
         lam = synth.make_lambdas(H, 0.99, 0.9999, seed=seed)
@@ -25,43 +24,66 @@ def _run(B, H, L, seed, lam=None, state=None, out_dtype=torch.float32):
     return y, st, y_ref, st_ref
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("L", [1, 5, 127, 128, 129, 300, 1000])
-def test_tc_lengths(L):
-    y, st, y_ref, st_ref = _run(2, 3, L, seed=L)
+def test_tc_lengths(L, D):
+    y, st, y_ref, st_ref = _run(2, 3, L, seed=L, D=D)
     assert_close(y, y_ref, TOL_BF16, "y")
     assert_state_close(st, st_ref, TOL_BF16)
 
 
-def test_tc_incoming_state_and_bf16_out():
+@pytest.mark.parametrize("D", [64, 128])
+def test_tc_incoming_state_and_bf16_out(D):
     B, H = 2, 4
     lam = torch.rand(B, H) * 0.02 + 0.98
-    st0 = synth.make_state(B, H, 64, lam[0], seed=3, t0=300, sigma=0.05, device="cuda")
-    y, st, y_ref, st_ref = _run(B, H, 517, seed=4, lam=lam, state=st0, out_dtype=torch.bfloat16)
+    st0 = synth.make_state(B, H, D, lam[0], seed=3, t0=300, sigma=0.05, device="cuda")
+    y, st, y_ref, st_ref = _run(B, H, 517, seed=4, lam=lam, state=st0, out_dtype=torch.bfloat16, D=D)
     assert_close(y, y_ref, TOL_BF16, "y")
     assert_state_close(st, st_ref, TOL_BF16)
 
 
-def test_tc_small_decay():
-    """Decays far from 1 (l^127 underflows toward zero): masks and weights stay finite."""
+@pytest.mark.parametrize("D", [64, 128])
+def test_tc_small_decay(D):
+    """Decays far from 1 (l^127 underflows toward zero): masks and weights stay finite; heads
+    below 0.55 take the float32 loop inside the same launch."""
     lam = torch.tensor([0.5, 0.1, 0.9])
-    y, st, y_ref, st_ref = _run(1, 3, 260, seed=7, lam=lam)
+    y, st, y_ref, st_ref = _run(1, 3, 260, seed=7, lam=lam, D=D)
     assert_close(y, y_ref, TOL_BF16, "y")
     assert_state_close(st, st_ref, TOL_BF16)
 
 
-def test_tc_segmented():
+@pytest.mark.parametrize("D", [64, 128])
+def test_tc_segmented(D):
     """B*H well below the SM count: sequences split into segments (state-only pass,
     prefix, full pass), all on the tensor-core kernel."""
     B, H, L = 1, 4, 4096 + 77
-    assert _lib.load().pma_prefill_workspace_bytes(B, H, L, 64, _lib.PMA_BF16) > 256
+    assert _lib.load().pma_prefill_workspace_bytes(B, H, L, D, _lib.PMA_BF16) > 256
     lam = torch.tensor([0.999, 0.99, 0.9999, 0.95])
-    st0 = synth.make_state(B, H, 64, lam, seed=8, t0=1000, sigma=0.02, device="cuda")
-    y, st, y_ref, st_ref = _run(B, H, L, seed=9, lam=lam, state=st0)
+    st0 = synth.make_state(B, H, D, lam, seed=8, t0=1000, sigma=0.02, device="cuda")
+    y, st, y_ref, st_ref = _run(B, H, L, seed=9, lam=lam, state=st0, D=D)
     assert_close(y, y_ref, TOL_BF16, "y")
     assert_state_close(st, st_ref, TOL_BF16)
-    q, k, v = synth.make_qkv(B, H, L, 64, seed=9, dtype=torch.bfloat16, device="cuda")
+    q, k, v = synth.make_qkv(B, H, L, D, seed=9, dtype=torch.bfloat16, device="cuda")
     _, st_only = ops.prefill(q, k, v, lam, state=st0, want_y=False, check=True)
     assert_state_close(st_only, st_ref, TOL_BF16, "state-only")
+
+
+def test_tc128_gqa_scale_strided():
+    """D = 128 through pma_prefill_ex: grouped k/v heads, a q scale exact in bf16 (applied by the
+    kernel), [B,L,H,D] views in and out."""
+    B, H, Hk, L, D = 2, 4, 2, 333, 128
+    g = torch.Generator().manual_seed(5)
+    qb = torch.nn.functional.normalize(torch.randn(B, L, H, D, generator=g), dim=-1).to("cuda", torch.bfloat16)
+    kvb = torch.nn.functional.normalize(torch.randn(B, L, 2 * Hk, D, generator=g), dim=-1).to("cuda", torch.bfloat16)
+    q, k, v = qb.transpose(1, 2), kvb[:, :, :Hk].transpose(1, 2), kvb[:, :, Hk:].transpose(1, 2)
+    lam = torch.tensor([0.999, 0.99, 0.98, 0.9995])
+    pro = ops.Prologue(kv_groups=2, q_scale=0.125)
+    y_bl = torch.empty(B, L, H, D, device="cuda", dtype=torch.float32)
+    _, st = ops.prefill(q, k, v, lam, y_out=y_bl.transpose(1, 2), prologue=pro, check=True)
+    k_r, v_r = k.repeat_interleave(2, dim=1), v.repeat_interleave(2, dim=1)
+    y_ref, st_ref = O.prefill((q.float() * 0.125).to(torch.bfloat16), k_r, v_r, lam_np(lam))
+    assert_close(y_bl.transpose(1, 2), y_ref, TOL_BF16, "y")
+    assert_state_close(st, st_ref, TOL_BF16)
 
 
 def test_tc_strided_module_layout():
