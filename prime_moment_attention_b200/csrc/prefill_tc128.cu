@@ -12,24 +12,33 @@
 //   dS   = KW^T V in two 128-feature halves (k, then k^2), K = 128 tokens  (:96-111)
 //   S    = l^n S + dS,  Z = l^n Z + sum_j KW_j,  S0 = l^n S0 + sum_j w_j v_j,  Z0 = l^n Z0 + sum_j w_j
 //                                                                          (:162-169)
-// The denominators (QQ_i.Z, sum_j P'_ij) and the column sums (dZ, dS0) are CUDA-core work; the
-// float32 state S1, S2 [128 x 128] lives in registers (thread (quadrant qd, quarter g, lane) owns
+// The column sums dZ = sum_j KW_j and dS0 = sum_j w_j v_j are N = 16 MMAs against a small operand
+// whose rows are [1 | w_hi | w_lo] (w = w_hi + w_lo in two bf16 parts, so dS0 keeps float32
+// weights), and the carry denominator QQ_i.Z one against the rows [Z_hi | Z_lo]; sum_j P'_ij is a
+// CUDA-core sum.  The float32 state S1, S2
+// [128 x 128] lives in registers (thread (quadrant qd, quarter g, lane) owns
 // feature row 32 qd + lane, value columns 32 g .. 32 g + 31 of both), Z, S0, Z0 in shared memory.
 // Head-states whose decay is below 0.55 (l^-128 would leave float32) run the float32 CUDA-core
 // chunk loop (prefill_simt_body.cuh) inside this kernel.
 //
 // Shared memory (~210 KB): q, k (-> w.k in place), w.k^2 and v as [128 tokens x 64] bf16 tiles with
 // the 128-byte swizzle (two per tensor: dims 0..63 and 64..127, each one TMA box), the bf16 state
-// [S1;S2] as two [256 features x 64 values] MN-major tiles, and the small vectors.
-// Tensor memory (512 columns): At / P' 0..127, dS 128..255, QQ 256..383, ACC 384..511.
+// [S1;S2] as two [256 features x 64 values] MN-major tiles, the [16 x 128 tokens] sums operand and
+// the [16 x 256 features] Z operand (both K-major), and the small vectors.
+// Tensor memory (512 columns): At / P' 0..127 (after P' is formed: dZ in 64 and 80, dS0 in 97 + 98,
+// QQ_i.Z in 112 + 113), dS 128..255, QQ 256..383, ACC 384..511.
 //
 // One CTA of 512 threads per (head-state, segment); the phases of a chunk are separated by
-// barriers and one thread issues the MMAs (two commit groups per chunk) and the TMA copies:
-//   P1  QQ -> tensor memory with QQ_i.Z, KW / KW.k in place with their column sums and those of w.v
-//   G1  At = QQ KW^T, dS = (w.k)^T V, ACC = QQ [S1;S2]    (then q of the next chunk is loaded)
-//   P3  P' and its row sums over At, S1 += dS
-//   G2  dS = (w.k^2)^T V, ACC += P' V                      (then k, v of the next chunk are loaded)
-//   P5  S2 += dS, the bf16 state tiles for the next chunk, the output rows
+// barriers.  Thread 0 issues the TMA copies; lane 0 of warp 12 issues the MMAs.  Each CUDA-core
+// phase waits only for the MMA group it reads and the groups that overlap it are issued at its
+// start: the issuing thread blocks while the tensor core's queue is full, and warp 12 has the
+// least CUDA-core work (its P' columns lie above the diagonal), so the other warps run meanwhile:
+//   P1  QQ -> tensor memory, KW / KW.k in place, the w rows of the sums operand
+//   M1  At = QQ KW^T, dS = (w.k)^T V                         (q of the next chunk is loaded)
+//   P3  [issue ACC = QQ [S1;S2]]  P' and its row sums over At, S1 += dS
+//   M2  dS = (w.k^2)^T V
+//   P5a [issue ACC += P' V, dZ, dS0, QQ.Z]  S2 += dS, the bf16 state tiles for the next chunk
+//   P5b Z (and its operand rows) and S0, the output rows     (k, v of the next chunk are loaded)
 // Every wait is bounded by the global timer; on expiry the kernel records a status code, leaves
 // the chunk loop on every thread, and waits (bounded) for its copies and MMAs in flight before
 // freeing tensor memory.
@@ -54,12 +63,17 @@ constexpr int OFF_K2 = 4 * TILE;        // w.k^2
 constexpr int OFF_V = 6 * TILE;         // v: values 0..63, then 64..127
 constexpr int OFF_SB = 8 * TILE;        // bf16 [S1;S2]: [256 features x 64 values] per value half
 constexpr int SB_HALF = 2 * TILE;
-constexpr int OFF_SMALL = OFF_SB + 2 * SB_HALF;
+constexpr int OFF_WT = OFF_SB + 2 * SB_HALF;  // sums operand: rows 1, w_hi, w_lo; two 64-token atoms
+constexpr int WT_ATOM = 2048;                  // [16 rows x 128 B] per atom
+constexpr int OFF_ZT = OFF_WT + 2 * WT_ATOM;  // Z operand: rows Z_hi, Z_lo; four 64-feature atoms
+constexpr int OFF_SMALL = OFF_ZT + 4 * WT_ATOM;
 constexpr int PREFETCH = 4;             // chunks of L2 prefetch ahead
 constexpr float LMIN = 0.55f;           // smallest decay the rescaled operands serve
 constexpr uint32_t T_AT = 0, T_DS = 128, T_QQ = 256, T_ACC = 384, T_COLS = 512;
+constexpr int ISSUER = 384;             // lane 0 of warp 12 (quadrant 0, columns 96..127)
 
-enum { B_FQ, B_FK, B_FV, B_MMA, NBAR };
+// copies: q, k, v tiles; MMA groups (committed once per chunk each; M1B only drained on the way out)
+enum { B_FQ, B_FK, B_FV, B_M1, B_M1B, B_M2, B_M3, NBAR };
 
 struct Small {
     uint64_t bar[NBAR];
@@ -71,10 +85,6 @@ struct Small {
     alignas(16) float zst[2 * D];       // Z = [Z1 ; Z2] entering the next P1
     alignas(16) float s0b[2][D];        // S0 entering the chunk, by chunk parity
     alignas(16) float z0b[4];           // Z0 entering the chunk, by chunk parity
-    alignas(16) float den[C];           // sum_j P'_ij + QQ_i.Z + Z0 per row
-    alignas(16) float zpart[4][2 * D];  // per token quarter: column sums of w.k | w.k^2
-    alignas(16) float s0part[4][D];     // per token quarter: column sums of w.v
-    alignas(16) float cdp[4][C];        // per feature quarter: partial QQ_i.Z
     alignas(16) float rsp[4][C];        // per column quarter: partial sum_j P'_ij
 };
 constexpr size_t TC_BYTES = OFF_SMALL + sizeof(Small);
@@ -97,32 +107,6 @@ __device__ __forceinline__ void store_row32<float>(float *dst, const float *v) {
     for (int c = 0; c < 8; ++c) d[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 }
 
-// Sum over the warp's 32 lanes of a[lane] (N = 32), or of a[lane >> 1] (N = 16): each level
-// exchanges half of the remaining values with the partner lane, so every lane ends with one
-// complete sum (31 or 16 shuffles instead of a butterfly per value).
-template <int N>
-__device__ __forceinline__ float reduce_scatter(float (&a)[32], int lane) {
-#pragma unroll
-    for (int lvl = 0; lvl < 5; ++lvl) {
-        const int o = 16 >> lvl;
-        const int half = (N >> 1) >> lvl;  // values kept after this level
-        if (half >= 1) {
-            const bool up = (lane & o) != 0;
-#pragma unroll
-            for (int m = 0; m < 16; ++m) {
-                if (m < half) {
-                    const float send = up ? a[m] : a[m + half];
-                    const float keep = up ? a[m + half] : a[m];
-                    a[m] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-                }
-            }
-        } else {
-            a[0] += __shfl_xor_sync(0xffffffffu, a[0], o);
-        }
-    }
-    return a[0];
-}
-
 __device__ __forceinline__ void load32(const float *src, float (&v)[32]) {
     const float4 *s = reinterpret_cast<const float4 *>(src);
 #pragma unroll
@@ -135,6 +119,26 @@ __device__ __forceinline__ void store32(float *dst, const float (&v)[32]) {
     float4 *d = reinterpret_cast<float4 *>(dst);
 #pragma unroll
     for (int c = 0; c < 8; ++c) d[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+
+// rows 0, 1 of the Z operand at feature f: Z_hi, Z_lo (K-major, 128-byte swizzle)
+__device__ __forceinline__ void put_z(uint8_t *zt, int f, float z) {
+    const __nv_bfloat16 hi = __float2bfloat16_rn(z);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(z - __bfloat162float(hi));
+    uint8_t *atom = zt + (f >> 6) * 2048;
+    const int c = (f & 63) >> 3, e = f & 7;
+    *reinterpret_cast<__nv_bfloat16 *>(atom + ((c ^ 0) << 4) + 2 * e) = hi;
+    *reinterpret_cast<__nv_bfloat16 *>(atom + 128 + ((c ^ 1) << 4) + 2 * e) = lo;
+}
+
+// two consecutive float32 columns of this thread's TMEM lane, with the wait
+__device__ __forceinline__ float2 tmem_ld2(uint32_t taddr) {
+    uint32_t a, b;
+    asm volatile("{\n\ttcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];\n\ttcgen05.wait::ld.sync.aligned;\n\t}"
+                 : "=r"(a), "=r"(b)
+                 : "r"(taddr)
+                 : "memory");
+    return make_float2(__uint_as_float(a), __uint_as_float(b));
 }
 
 // bounded wait used only on the way out (copies or MMAs that may still be in flight)
@@ -205,6 +209,12 @@ __global__ void __launch_bounds__(NT, 1)
         if (tid < D) sm.s0b[0][tid] = 0.f;
         if (tid == 0) sm.z0b[0] = 0.f;
     }
+    for (int i = tid; i < 6 * WT_ATOM / 16; i += NT) {  // sums operand: row 0 ones; the rest zero
+        const int r = (i >> 3) & 15;
+        const uint32_t one2 = 0x3F803F80u;
+        *reinterpret_cast<uint4 *>(smem + OFF_WT + 16 * i) =
+            (r == 0 && i < 2 * WT_ATOM / 16) ? make_uint4(one2, one2, one2, one2) : make_uint4(0u, 0u, 0u, 0u);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -228,7 +238,10 @@ __global__ void __launch_bounds__(NT, 1)
             *reinterpret_cast<uint4 *>(tile + swz(D + fl, c0 + c)) = pack8(S2r + 8 * c);
         }
     };
-    if (!SO) publish();
+    if (!SO) {
+        publish();
+        if (tid < 2 * D) put_z(smem + OFF_ZT, tid, sm.zst[tid]);
+    }
 
     // ---- copies (thread 0)
     auto load_tile2 = [&](int off, const CUtensorMap *map, uint64_t *bb, int t0, int hh) {
@@ -255,8 +268,10 @@ __global__ void __launch_bounds__(NT, 1)
         load_tile2(OFF_V, &tv, &bar[B_FV], t0, hk);
     }
     // phases of the four barriers, and which of them have an operation in flight
-    uint32_t ph_q = 0, ph_k = 0, ph_v = 0, ph_m = 0;
-    bool pend_q = !SO && U > 0, pend_k = U > 0, pend_v = U > 0, pend_m = false;
+    uint32_t ph_q = 0, ph_k = 0, ph_v = 0;
+    bool pend_q = !SO && U > 0, pend_k = U > 0, pend_v = U > 0;
+    int pend_m = -1;           // latest MMA commit not yet waited for (it covers every earlier MMA)
+    uint32_t pend_par = 0;
     fence_proxy_async();  // the state tiles are read by the tensor core
     __syncthreads();
 
@@ -264,6 +279,8 @@ __global__ void __launch_bounds__(NT, 1)
     constexpr uint32_t ID_SC = idesc(128, 128, 0, 0);  // QQ (tmem) KW^T
     constexpr uint32_t ID_DS = idesc(128, 128, 1, 1);  // (w.k)^T V: both MN-major
     constexpr uint32_t ID_TV = idesc(128, 128, 0, 1);  // QQ [S1;S2], P' V: B MN-major
+    constexpr uint32_t ID_CS = idesc(128, 16, 1, 0);   // column sums: A MN-major, B K-major
+    constexpr uint32_t ID_CZ = idesc(128, 16, 0, 0);   // QQ (tmem) [Z_hi | Z_lo]
     constexpr uint64_t HI_KMAJ = desc_hi(16, 1024, 2);       // K-major, 128 B rows
     constexpr uint64_t HI_TILE2 = desc_hi(TILE, 1024, 2);    // MN-major, second 64-wide atom one tile on
     constexpr uint64_t HI_SB = desc_hi(SB_HALF, 1024, 2);    // MN-major state tiles
@@ -291,11 +308,9 @@ __global__ void __launch_bounds__(NT, 1)
         ph_k ^= 1;
         ph_v ^= 1;
         pend_k = pend_v = false;
-        if (!SO) {  // QQ row fl, features 64 g .. 64 g + 63 (tensor-memory columns 32 g ..), and QQ_i.Z
+        if (!SO) {  // QQ row fl, features 64 g .. 64 g + 63 (tensor-memory columns 32 g ..)
             const uint8_t *qs = smem + OFF_Q + (g & 1) * TILE;
-            const float *zf = sm.zst + 64 * g;
             const __nv_bfloat162 half2 = __float2bfloat162_rn(0.5f);
-            float cd = 0.f;
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
                 uint32_t r[16];
@@ -316,25 +331,19 @@ __global__ void __launch_bounds__(NT, 1)
                             x = as_u(__hmul2(qv, __hmul2(qv, half2)));
                         }
                         r[4 * c + t] = x;
-                        const float2 qf = bf2f(x);
-                        const float2 zz = *reinterpret_cast<const float2 *>(zf + 32 * hh + 8 * c + 2 * t);
-                        cd = fmaf(qf.x, zz.x, fmaf(qf.y, zz.y, cd));
                     }
                 }
                 tmem_st16(lane_base + T_QQ + 32 * g + 16 * hh, r);
             }
-            sm.cdp[g][fl] = cd;
         }
-        {  // KW = w.k in place, K2W = KW.k; column sums of both (dims 16 dg .. 16 dg + 15) and of w.v
+        {  // KW = w.k in place, K2W = KW.k (dims 16 dg .. 16 dg + 15 of token fl, dg = g, g + 4)
             const float wj = fl < n ? sm.pw[n - 1 - fl] : 0.f;
             const __nv_bfloat162 wb = __float2bfloat162_rn(wj);
-#pragma unroll 1
+#pragma unroll
             for (int it = 0; it < 2; ++it) {
                 const int dg = g + 4 * it;
                 uint8_t *ks = smem + OFF_K + (dg >> 2) * TILE;
                 uint8_t *k2s = smem + OFF_K2 + (dg >> 2) * TILE;
-                const uint8_t *vs = smem + OFF_V + (dg >> 2) * TILE;
-                float a[32];
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
                     const uint32_t off = swz(fl, 2 * (dg & 3) + cc);
@@ -347,30 +356,18 @@ __global__ void __launch_bounds__(NT, 1)
                         const __nv_bfloat162 kw = __hmul2(kv, wb);
                         o1[c] = as_u(kw);
                         o2[c] = as_u(__hmul2(kw, kv));
-                        const float2 f1 = bf2f(o1[c]), f2 = bf2f(o2[c]);
-                        a[8 * cc + 2 * c] = f1.x;
-                        a[8 * cc + 2 * c + 1] = f1.y;
-                        a[16 + 8 * cc + 2 * c] = f2.x;
-                        a[16 + 8 * cc + 2 * c + 1] = f2.y;
                     }
                     *reinterpret_cast<uint4 *>(ks + off) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
                     *reinterpret_cast<uint4 *>(k2s + off) = make_uint4(o2[0], o2[1], o2[2], o2[3]);
                 }
-                const float s = reduce_scatter<32>(a, lane);  // lane < 16: w.k of dim 16 dg + lane, else w.k^2
-                sm.zpart[qd][lane < 16 ? 16 * dg + lane : D + 16 * dg + lane - 16] = s;
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const uint4 x = *reinterpret_cast<const uint4 *>(vs + swz(fl, 2 * (dg & 3) + cc));
-                    const uint32_t e4[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const float2 f = bf2f(e4[c]);
-                        a[8 * cc + 2 * c] = wj * f.x;
-                        a[8 * cc + 2 * c + 1] = wj * f.y;
-                    }
-                }
-                const float s0 = reduce_scatter<16>(a, lane);  // value 16 dg + lane / 2
-                if ((lane & 1) == 0) sm.s0part[qd][16 * dg + (lane >> 1)] = s0;
+            }
+            if (tid < C) {  // w_hi, w_lo of token tid: rows 1, 2 of the sums operand (K-major, swizzled)
+                const __nv_bfloat16 whi = __float2bfloat16_rn(wj);
+                const __nv_bfloat16 wlo = __float2bfloat16_rn(wj - __bfloat162float(whi));
+                uint8_t *atom = smem + OFF_WT + (tid >> 6) * WT_ATOM;
+                const int c = (tid & 63) >> 3, e = tid & 7;
+                *reinterpret_cast<__nv_bfloat16 *>(atom + 1 * 128 + ((c ^ 1) << 4) + 2 * e) = whi;
+                *reinterpret_cast<__nv_bfloat16 *>(atom + 2 * 128 + ((c ^ 2) << 4) + 2 * e) = wlo;
             }
         }
         if (!SO) tmem_wait_st();
@@ -379,8 +376,8 @@ __global__ void __launch_bounds__(NT, 1)
         __syncthreads();
         tc_fence_after();
 
-        // ================= G1: At = QQ KW^T, dS = (w.k)^T V, ACC = QQ [S1;S2]
-        if (tid == 0) {
+        // ================= M1: At = QQ KW^T, dS = (w.k)^T V
+        if (tid == ISSUER) {
             if (!SO) {
 #pragma unroll
                 for (int k = 0; k < 16; ++k) {  // K = features: w.k dims 0..63, 64..127, then w.k^2
@@ -393,38 +390,36 @@ __global__ void __launch_bounds__(NT, 1)
             for (int k = 0; k < 8; ++k)  // K = tokens, 16 rows = 2048 B per step
                 mma_ss(tmem + T_DS, dsc(OFF_K, HI_TILE2) + (uint64_t)(k * 128), dsc(OFF_V, HI_TILE2) + (uint64_t)(k * 128),
                        ID_DS, k > 0);
-            if (!SO) {
-#pragma unroll
-                for (int k = 0; k < 16; ++k)  // K = features, 16 rows of the state tiles per step
-                    mma_ts(tmem + T_ACC, tmem + T_QQ + 8 * k, dsc(OFF_SB, HI_SB) + (uint64_t)(k * 128), ID_TV, k > 0);
-            }
-            commit(&bar[B_MMA]);
+            commit(&bar[B_M1]);
+        }
+        if (tid == 0) {
             // the q tiles are consumed (QQ is in tensor memory): the next chunk's q lands now
             if (!SO && u + 1 < U) load_tile2(OFF_Q, &tq, &bar[B_FQ], (c_begin + u + 1) * C, h);
             prefetch_to(u + 1 + PREFETCH);
         }
-        pend_m = true;
+        pend_m = B_M1;
+        pend_par = par;
         if (!SO && u + 1 < U) pend_q = true;
-        // while G1 runs: the state vectors (QQ_i.Z above used Z entering this chunk)
-        if (tid < 2 * D)
-            sm.zst[tid] = fmaf(dec, sm.zst[tid],
-                               (sm.zpart[0][tid] + sm.zpart[1][tid]) + (sm.zpart[2][tid] + sm.zpart[3][tid]));
-        if (tid < D)
-            sm.s0b[par ^ 1][tid] = fmaf(dec, sm.s0b[par][tid],
-                                        (sm.s0part[0][tid] + sm.s0part[1][tid]) + (sm.s0part[2][tid] + sm.s0part[3][tid]));
         if (tid == 0) sm.z0b[par ^ 1] = fmaf(dec, sm.z0b[par], sm.geo[n]);
         {
-            const bool w = mbar_wait(&bar[B_MMA], ph_m, ctl, 34);
+            const bool w = mbar_wait(&bar[B_M1], par, ctl, 34);
             if (!__syncthreads_and(w)) {
                 ok = false;
                 break;
             }
         }
-        ph_m ^= 1;
-        pend_m = false;
         tc_fence_after();
 
         // ================= P3: P' over At (row fl, columns 32 g ..), S1 += dS
+        if (tid == ISSUER) {  // the carry GEMM runs under this phase
+            if (!SO) {
+#pragma unroll
+                for (int k = 0; k < 16; ++k)  // K = features, 16 rows of the state tiles per step
+                    mma_ts(tmem + T_ACC, tmem + T_QQ + 8 * k, dsc(OFF_SB, HI_SB) + (uint64_t)(k * 128), ID_TV, k > 0);
+            }
+            commit(&bar[B_M1B]);
+        }
+        pend_m = B_M1B;
         if (!SO) {
             const bool live = g <= qd;  // columns past the row quadrant are all masked
             uint32_t pk[16];
@@ -471,53 +466,96 @@ __global__ void __launch_bounds__(NT, 1)
         __syncthreads();
         tc_fence_after();
 
-        // ================= G2: dS = (w.k^2)^T V, ACC += P' V
-        if (tid == 0) {
+        // ================= M2: dS = (w.k^2)^T V (its commit also covers the carry GEMM)
+        if (tid == ISSUER) {
 #pragma unroll
             for (int k = 0; k < 8; ++k)
                 mma_ss(tmem + T_DS, dsc(OFF_K2, HI_TILE2) + (uint64_t)(k * 128),
                        dsc(OFF_V, HI_TILE2) + (uint64_t)(k * 128), ID_DS, k > 0);
-            if (!SO) {
-#pragma unroll
-                for (int k = 0; k < 8; ++k)  // K = tokens; P' packs 2 per column
-                    mma_ts(tmem + T_ACC, tmem + T_AT + 8 * k, dsc(OFF_V, HI_TILE2) + (uint64_t)(k * 128), ID_TV, 1);
-            }
-            commit(&bar[B_MMA]);
+            commit(&bar[B_M2]);
         }
-        pend_m = true;
-        if (!SO && tid < C)
-            sm.den[tid] = ((sm.rsp[0][tid] + sm.rsp[1][tid]) + (sm.rsp[2][tid] + sm.rsp[3][tid])) +
-                          ((sm.cdp[0][tid] + sm.cdp[1][tid]) + (sm.cdp[2][tid] + sm.cdp[3][tid])) + sm.z0b[par];
+        pend_m = B_M2;
         {
-            const bool w = mbar_wait(&bar[B_MMA], ph_m, ctl, 35);
+            const bool w = mbar_wait(&bar[B_M2], par, ctl, 35);
             if (!__syncthreads_and(w)) {
                 ok = false;
                 break;
             }
         }
-        ph_m ^= 1;
-        pend_m = false;
         tc_fence_after();
 
-        // ================= P5: S2 += dS, next chunk's k / v and state tiles, output rows
-        if (tid == 0 && u + 1 < U) {  // every GEMM of this chunk is complete: k, v tiles are free
-            const int t1 = (c_begin + u + 1) * C;
-            load_tile2(OFF_K, &tk, &bar[B_FK], t1, hk);
-            load_tile2(OFF_V, &tv, &bar[B_FV], t1, hk);
+        // ================= P5a: S2 += dS, the state tiles for the next chunk (the carry GEMM is done)
+        if (tid == ISSUER) {  // M3 runs under this phase: ACC += P' V, column sums into free At columns
+            if (!SO) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k)  // K = tokens; P' packs 2 per column
+                    mma_ts(tmem + T_ACC, tmem + T_AT + 8 * k, dsc(OFF_V, HI_TILE2) + (uint64_t)(k * 128), ID_TV, 1);
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {  // [w.k | w.k^2 | v]^T [1 | w_hi | w_lo]
+                const uint64_t bw = dsc(OFF_WT + (k >> 2) * WT_ATOM, HI_KMAJ) + (uint64_t)((k & 3) * 2);
+                const uint64_t mk = (uint64_t)(k * 128);
+                mma_ss(tmem + T_AT + 64, dsc(OFF_K, HI_TILE2) + mk, bw, ID_CS, k > 0);
+                mma_ss(tmem + T_AT + 80, dsc(OFF_K2, HI_TILE2) + mk, bw, ID_CS, k > 0);
+                mma_ss(tmem + T_AT + 96, dsc(OFF_V, HI_TILE2) + mk, bw, ID_CS, k > 0);
+            }
+            if (!SO) {
+#pragma unroll
+                for (int k = 0; k < 16; ++k)  // QQ [Z_hi | Z_lo]: K = features
+                    mma_ts(tmem + T_AT + 112, tmem + T_QQ + 8 * k,
+                           dsc(OFF_ZT + (k >> 2) * WT_ATOM, HI_KMAJ) + (uint64_t)((k & 3) * 2), ID_CZ, k > 0);
+            }
+            commit(&bar[B_M3]);
         }
-        if (u + 1 < U) pend_k = pend_v = true;
+        pend_m = B_M3;
         {
             float ds[32];
             tmem_ld32(lane_base + T_DS + 32 * g, ds);
 #pragma unroll
             for (int e = 0; e < 32; ++e) S2r[e] = fmaf(dec, S2r[e], ds[e]);
         }
+        if (!SO && u + 1 < U) {
+            publish();
+            fence_proxy_async();  // the state tiles are read by the next carry GEMM
+        }
+        {
+            const bool w = mbar_wait(&bar[B_M3], par, ctl, 36);
+            if (!__syncthreads_and(w)) {
+                ok = false;
+                break;
+            }
+        }
+        pend_m = -1;
+        tc_fence_after();
+
+        // ================= P5b: next chunk's k / v, Z and S0, output rows
+        if (tid == 0 && u + 1 < U) {  // every GEMM of this chunk is complete: k, v tiles are free
+            const int t1 = (c_begin + u + 1) * C;
+            load_tile2(OFF_K, &tk, &bar[B_FK], t1, hk);
+            load_tile2(OFF_V, &tv, &bar[B_FV], t1, hk);
+        }
+        if (u + 1 < U) pend_k = pend_v = true;
+        if (g < 2) {  // Z1 / Z2 of feature fl (column 0 of the sums: the ones row)
+            const float dz = tmem_ld1(lane_base + T_AT + 64 + 16 * g);
+            const float z = fmaf(dec, sm.zst[D * g + fl], dz);
+            sm.zst[D * g + fl] = z;
+            if (!SO && u + 1 < U) {
+                put_z(smem + OFF_ZT, D * g + fl, z);
+                fence_proxy_async();  // read by the next chunk's QQ.Z GEMM
+            }
+        } else if (g == 2) {  // S0 of value fl: the w_hi and w_lo columns
+            const float hi = tmem_ld1(lane_base + T_AT + 97);
+            const float lo = tmem_ld1(lane_base + T_AT + 98);
+            sm.s0b[par ^ 1][fl] = fmaf(dec, sm.s0b[par][fl], hi + lo);
+        }
         if (!SO) {
-            if (u + 1 < U) publish();
             float acc[32];
             tmem_ld32(lane_base + T_ACC + 32 * g, acc);
+            const float2 cz = tmem_ld2(lane_base + T_AT + 112);  // QQ_i.Z_hi, QQ_i.Z_lo
+            const float den = ((sm.rsp[0][fl] + sm.rsp[1][fl]) + (sm.rsp[2][fl] + sm.rsp[3][fl])) + (cz.x + cz.y) +
+                              sm.z0b[par];
             const float gi = sm.pw[fl + 1];
-            const float sc = gi / fmaxf(gi * sm.den[fl], p.eps);
+            const float sc = gi / fmaxf(gi * den, p.eps);
             const float *s0v = sm.s0b[par] + 32 * g;
 #pragma unroll
             for (int e = 0; e < 32; ++e) acc[e] = (acc[e] + s0v[e]) * sc;
@@ -527,7 +565,6 @@ __global__ void __launch_bounds__(NT, 1)
                 store_row32<TO>(yrow, acc);
             }
         }
-        fence_proxy_async();  // the state tiles are read by the next G1
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
@@ -538,7 +575,7 @@ __global__ void __launch_bounds__(NT, 1)
         if (pend_q) drain(&bar[B_FQ], ph_q);
         if (pend_k) drain(&bar[B_FK], ph_k);
         if (pend_v) drain(&bar[B_FV], ph_v);
-        if (pend_m) drain(&bar[B_MMA], ph_m);
+        if (pend_m >= 0) drain(&bar[pend_m], pend_par);
     }
     // ---- final state
     const bool write_out = ok && !*ctl.abort_flag && p.out.present() &&
