@@ -67,7 +67,10 @@ constexpr int OFF_WT = OFF_SB + 2 * SB_HALF;  // sums operand: rows 1, w_hi, w_l
 constexpr int WT_ATOM = 2048;                  // [16 rows x 128 B] per atom
 constexpr int OFF_ZT = OFF_WT + 2 * WT_ATOM;  // Z operand: rows Z_hi, Z_lo; four 64-feature atoms
 constexpr int OFF_SMALL = OFF_ZT + 4 * WT_ATOM;
-constexpr int PREFETCH = 4;             // chunks of L2 prefetch ahead
+// L2 prefetch of the next chunk only (issued with its q copy): prefetching 4 chunks ahead raised
+// the full pass's DRAM reads to 1.86x the bytes of q, k, v (lines evicted before their copy ran)
+// and did not shorten it.
+constexpr int PREFETCH = 0;
 constexpr float LMIN = 0.55f;           // smallest decay the rescaled operands serve
 constexpr uint32_t T_AT = 0, T_DS = 128, T_QQ = 256, T_ACC = 384, T_COLS = 512;
 constexpr int ISSUER = 384;             // lane 0 of warp 12 (quadrant 0, columns 96..127)

@@ -57,7 +57,7 @@ def _worker(rank, world, port, D, dtype_name, out):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("D,dtype_name,tol", [(64, "bfloat16", TOL_BF16), (64, "float32", TOL_F32),
-                                              (128, "float32", TOL_F32)])
+                                              (128, "bfloat16", TOL_BF16), (128, "float32", TOL_F32)])
 def test_sequence_parallel_prefill_nccl(D, dtype_name, tol):
     world = min(torch.cuda.device_count(), 4)
     out = mp.Manager().dict()
