@@ -39,6 +39,7 @@ def _seq(t):
 @pytest.mark.parametrize("dtype,B,H,L,D", [
     (torch.bfloat16, 1, 4, 4173, 64),   # tensor-core kernel, split into segments (scratch holds their states)
     (torch.bfloat16, 2, 3, 300, 64),    # tensor-core kernel, status word only
+    (torch.bfloat16, 1, 4, 2000, 128),  # head-dim-128 tensor-core kernel, segmented
     (torch.float32, 1, 2, 1000, 32),    # CUDA-core kernel, segmented
 ])
 def test_no_alloc_matches_workspace_entry_point(dtype, B, H, L, D):
