@@ -39,6 +39,9 @@
 //   M2  dS = (w.k^2)^T V
 //   P5a [issue ACC += P' V, dZ, dS0, QQ.Z]  S2 += dS, the bf16 state tiles for the next chunk
 //   P5b Z (and its operand rows) and S0, the output rows     (k, v of the next chunk are loaded)
+// The state-only pass (the segment carry's first launch) has no q, P', carry or output: after P1 it
+// runs one MMA group, dS = (w.k | w.k^2)^T [V | 1] (N = 144: a ones tile in the unused state-tile
+// space gives dZ as column 128) and dS0, then the state update.
 // Every wait is bounded by the global timer; on expiry the kernel records a status code, leaves
 // the chunk loop on every thread, and waits (bounded) for its copies and MMAs in flight before
 // freeing tensor memory.
@@ -244,6 +247,11 @@ __global__ void __launch_bounds__(NT, 1)
     if (!SO) {
         publish();
         if (tid < 2 * D) put_z(smem + OFF_ZT, tid, sm.zst[tid]);
+    } else {  // state only: the ones tile [128 tokens x 64], column 0 = 1, in the unused state-tile space
+        for (int i = tid; i < TILE / 16; i += NT) {
+            const int r = i >> 3, c = i & 7;  // element 0 of row r sits in chunk 0 ^ (r & 7)
+            *reinterpret_cast<uint4 *>(smem + OFF_SB + 16 * i) = make_uint4(c == (r & 7) ? 0x3F80u : 0u, 0u, 0u, 0u);
+        }
     }
 
     // ---- copies (thread 0)
@@ -284,6 +292,7 @@ __global__ void __launch_bounds__(NT, 1)
     constexpr uint32_t ID_TV = idesc(128, 128, 0, 1);  // QQ [S1;S2], P' V: B MN-major
     constexpr uint32_t ID_CS = idesc(128, 16, 1, 0);   // column sums: A MN-major, B K-major
     constexpr uint32_t ID_CZ = idesc(128, 16, 0, 0);   // QQ (tmem) [Z_hi | Z_lo]
+    constexpr uint32_t ID_DZ = idesc(128, 144, 1, 1);  // state only: (w.k)^T [V | 1]
     constexpr uint64_t HI_KMAJ = desc_hi(16, 1024, 2);       // K-major, 128 B rows
     constexpr uint64_t HI_TILE2 = desc_hi(TILE, 1024, 2);    // MN-major, second 64-wide atom one tile on
     constexpr uint64_t HI_SB = desc_hi(SB_HALF, 1024, 2);    // MN-major state tiles
@@ -378,6 +387,65 @@ __global__ void __launch_bounds__(NT, 1)
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
+
+        if constexpr (SO) {
+            // ================= state only: one MMA group per chunk.  dS = (w.k | w.k^2)^T [V | 1]
+            // (N = 144: the ones tile, in the state-tile space this mode leaves unused, is V's third
+            // N-atom, so column 128 of each result is dZ) and dS0 = v^T [1 | w_hi | w_lo].
+            if (tid == ISSUER) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {  // K = tokens, 16 rows = 2048 B per step
+                    const uint64_t mk = (uint64_t)(k * 128);
+                    mma_ss(tmem + T_DS, dsc(OFF_K, HI_TILE2) + mk, dsc(OFF_V, HI_TILE2) + mk, ID_DZ, k > 0);
+                    mma_ss(tmem + T_DS + 144, dsc(OFF_K2, HI_TILE2) + mk, dsc(OFF_V, HI_TILE2) + mk, ID_DZ, k > 0);
+                    mma_ss(tmem + T_AT + 96, dsc(OFF_V, HI_TILE2) + mk,
+                           dsc(OFF_WT + (k >> 2) * WT_ATOM, HI_KMAJ) + (uint64_t)((k & 3) * 2), ID_CS, k > 0);
+                }
+                commit(&bar[B_M1]);
+            }
+            pend_m = B_M1;
+            pend_par = par;
+            if (tid == 0) {
+                sm.z0b[par ^ 1] = fmaf(dec, sm.z0b[par], sm.geo[n]);
+                prefetch_to(u + 1 + PREFETCH);
+            }
+            {
+                const bool w = mbar_wait(&bar[B_M1], par, ctl, 37);
+                if (!__syncthreads_and(w)) {
+                    ok = false;
+                    break;
+                }
+            }
+            pend_m = -1;
+            tc_fence_after();
+            if (tid == 0 && u + 1 < U) {  // every GEMM of this chunk is complete: k, v tiles are free
+                const int t1 = (c_begin + u + 1) * C;
+                load_tile2(OFF_K, &tk, &bar[B_FK], t1, hk);
+                load_tile2(OFF_V, &tv, &bar[B_FV], t1, hk);
+            }
+            if (u + 1 < U) pend_k = pend_v = true;
+            {
+                float ds[32];
+                tmem_ld32(lane_base + T_DS + 32 * g, ds);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) S1r[e] = fmaf(dec, S1r[e], ds[e]);
+                tmem_ld32(lane_base + T_DS + 144 + 32 * g, ds);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) S2r[e] = fmaf(dec, S2r[e], ds[e]);
+            }
+            if (g < 2) {  // Z1 / Z2 of feature fl: the ones column of each dS
+                const float dz = tmem_ld1(lane_base + T_DS + 144 * g + 128);
+                sm.zst[D * g + fl] = fmaf(dec, sm.zst[D * g + fl], dz);
+            } else if (g == 2) {  // S0 of value fl: the w_hi and w_lo columns
+                const float hi = tmem_ld1(lane_base + T_AT + 97);
+                const float lo = tmem_ld1(lane_base + T_AT + 98);
+                sm.s0b[par ^ 1][fl] = fmaf(dec, sm.s0b[par][fl], hi + lo);
+            }
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            continue;
+        }
 
         // ================= M1: At = QQ KW^T, dS = (w.k)^T V
         if (tid == ISSUER) {
