@@ -38,7 +38,8 @@
 //   P3  [issue ACC = QQ [S1;S2]]  P' and its row sums over At, S1 += dS
 //   M2  dS = (w.k^2)^T V
 //   P5a [issue ACC += P' V, dZ, dS0, QQ.Z]  S2 += dS, the bf16 state tiles for the next chunk
-//   P5b Z (and its operand rows) and S0, the output rows     (k, v of the next chunk are loaded)
+//   P5b Z (and its operand rows) and S0, the rows' denominators (k, v of the next chunk are loaded)
+// and the output rows of chunk u run in chunk u+1's M1 window (ACC is untouched until its P3).
 // The state-only pass (the segment carry's first launch) has no q, P', carry or output: after P1 it
 // runs one MMA group, dS = (w.k | w.k^2)^T [V | 1] (N = 144: a ones tile in the unused state-tile
 // space gives dZ as column 128) and dS0, then the state update.
@@ -299,6 +300,25 @@ __global__ void __launch_bounds__(NT, 1)
     const uint32_t a0 = sb >> 4;  // the allocation sits below 256 KiB: no field overflow
     auto dsc = [&](uint32_t off, uint64_t hi) { return (uint64_t)(a0 + (off >> 4)) | hi; };
 
+    // Output rows of chunk uo from ACC (which no GEMM touches until the next chunk's carry GEMM is
+    // issued in its P3): they run in the next chunk's M1 window, or after the loop for the last one.
+    float den_prev = 0.f;
+    auto output_rows = [&](int uo) {
+        const int no = (uo == U - 1) ? n_last : C;
+        float acc[32];
+        tmem_ld32(lane_base + T_ACC + 32 * g, acc);
+        const float gi = sm.pw[fl + 1];
+        const float sc = gi / fmaxf(gi * den_prev, p.eps);
+        const float *s0v = sm.s0b[uo & 1] + 32 * g;  // S0 entering chunk uo
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[e] = (acc[e] + s0v[e]) * sc;
+        if (fl < no) {
+            TO *yrow = reinterpret_cast<TO *>(p.y.p) + b * p.y.sb + h * p.y.sh +
+                       (int64_t)((c_begin + uo) * C + fl) * p.y.sl + 32 * g;
+            store_row32<TO>(yrow, acc);
+        }
+    };
+
     bool ok = true;
     for (int u = 0; u < U && ok; ++u) {
         const int n = (u == U - 1) ? n_last : C;
@@ -472,7 +492,9 @@ __global__ void __launch_bounds__(NT, 1)
         pend_par = par;
         if (!SO && u + 1 < U) pend_q = true;
         if (tid == 0) sm.z0b[par ^ 1] = fmaf(dec, sm.z0b[par], sm.geo[n]);
+        if (!SO && u > 0) output_rows(u - 1);  // under the score and dS GEMMs
         {
+            tc_fence_before();  // the ACC reads above precede this chunk's carry GEMM
             const bool w = mbar_wait(&bar[B_M1], par, ctl, 34);
             if (!__syncthreads_and(w)) {
                 ok = false;
@@ -619,28 +641,20 @@ __global__ void __launch_bounds__(NT, 1)
             const float lo = tmem_ld1(lane_base + T_AT + 98);
             sm.s0b[par ^ 1][fl] = fmaf(dec, sm.s0b[par][fl], hi + lo);
         }
-        if (!SO) {
-            float acc[32];
-            tmem_ld32(lane_base + T_ACC + 32 * g, acc);
+        if (!SO) {  // row fl's denominator (its QQ.Z columns are overwritten by the next score GEMM)
             const float2 cz = tmem_ld2(lane_base + T_AT + 112);  // QQ_i.Z_hi, QQ_i.Z_lo
-            const float den = ((sm.rsp[0][fl] + sm.rsp[1][fl]) + (sm.rsp[2][fl] + sm.rsp[3][fl])) + (cz.x + cz.y) +
-                              sm.z0b[par];
-            const float gi = sm.pw[fl + 1];
-            const float sc = gi / fmaxf(gi * den, p.eps);
-            const float *s0v = sm.s0b[par] + 32 * g;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) acc[e] = (acc[e] + s0v[e]) * sc;
-            if (fl < n) {
-                TO *yrow = reinterpret_cast<TO *>(p.y.p) + b * p.y.sb + h * p.y.sh +
-                           (int64_t)((c_begin + u) * C + fl) * p.y.sl + 32 * g;
-                store_row32<TO>(yrow, acc);
-            }
+            den_prev = ((sm.rsp[0][fl] + sm.rsp[1][fl]) + (sm.rsp[2][fl] + sm.rsp[3][fl])) + (cz.x + cz.y) +
+                       sm.z0b[par];
         }
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
     }
 
+    if (!SO && ok && U > 0) {
+        tc_fence_after();
+        output_rows(U - 1);
+    }
     // ---- never leave with copies or GEMMs in flight (only a failed wait leaves any)
     if (tid == 0) {
         if (pend_q) drain(&bar[B_FQ], ph_q);
