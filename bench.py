@@ -536,6 +536,12 @@ def bench_sp(args, ws, rank, device, stream, peaks):
     tokheads = c["B"] * c["L"] * c["H"]
     tf = tokheads * SP_FLOP_PER_TOKHEAD / (ms * 1e-3) / 1e12
     bw = tokheads * SP_BYTES_PER_TOKHEAD / (ms * 1e-3) / 1e9
+    # this package's kernel launches per step (the plan splits a long shard into segments: a
+    # state-only pass, the segment prefix and the full pass); with shards, the last rank also runs
+    # the state-only prefill of its shard (pass + prefix) and one state combine per earlier shard
+    from prime_moment_attention_b200 import _lib
+    seg = _lib.load().pma_prefill_workspace_bytes(c["B"], c["H"], Ls, c["D"], _lib.PMA_BF16) > 256
+    per_step = (3 if seg else 1) if ws == 1 else (2 if seg else 1) + (ws - 1) + (3 if seg else 1)
     return {"metric": "sp_prefill_tok_per_s", "value": round(c["B"] * c["L"] / (ms * 1e-3), 1), "unit": "tok/s",
             "ms_per_step": round(ms, 3), "steps": steps, "higher_is_better": True, "scaling": "strong",
             "dtype": "bf16",
@@ -550,7 +556,7 @@ def bench_sp(args, ws, rank, device, stream, peaks):
                                     "frac": round(tf / (peaks[1] * ws), 4)},
                          "algorithmic_bytes_per_step": tokheads * SP_BYTES_PER_TOKHEAD,
                          "algorithmic_flop_per_step": tokheads * SP_FLOP_PER_TOKHEAD},
-            "gpu_launches": None, "clocks": clk_r}
+            "gpu_launches": steps * per_step, "clocks": clk_r}
 
 
 def bench_selective(args, ws, rank, device, stream, peaks):
