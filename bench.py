@@ -122,8 +122,11 @@ def dist_setup():
     if ws > 1:
         import datetime
         import torch.distributed as dist
-        # NCCL's own log lines (its version banner under NCCL_DEBUG=VERSION) go to stderr, so that
-        # rank 0's stdout carries the one JSON line only
+        # NCCL's own log lines go to stderr, so that rank 0's stdout carries the one JSON line only.
+        # NCCL honours NCCL_DEBUG_FILE only above the VERSION level (at VERSION its banner goes to
+        # stdout), so VERSION is raised to WARN, which prints the same banner plus warnings.
+        if os.environ.get("NCCL_DEBUG", "").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
