@@ -221,6 +221,97 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
     return y, st_out_t
 
 
+_copy_streams = {}
+_host_staging = {}  # device index -> (key, (q, k, v, y) device staging buffers)
+
+
+def release_host_staging():
+    """Free the device staging buffers that prefill_from_host keeps between calls."""
+    _host_staging.clear()
+
+
+def _staging(dev, q, k, v, y_dtype):
+    """Device buffers for prefill_from_host, kept per device for the last shapes used (reusing them
+    avoids an allocation per call; call order on the streams keeps successive calls apart)."""
+    key = (tuple(q.shape), tuple(k.shape), tuple(v.shape), q.dtype, y_dtype)
+    hit = _host_staging.get(dev.index)
+    if hit is None or hit[0] != key:
+        _host_staging.pop(dev.index, None)
+        bufs = tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in (q, k, v))
+        bufs += (torch.empty(q.shape, dtype=y_dtype, device=dev),)
+        hit = (key, bufs)
+        _host_staging[dev.index] = hit
+    return hit[1]
+
+
+def _copy_stream_pair(device):
+    """Two side streams per device (host->device, device->host), created once."""
+    key = torch.device(device).index
+    pair = _copy_streams.get(key)
+    if pair is None:
+        pair = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+        _copy_streams[key] = pair
+    return pair
+
+
+def prefill_from_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay, device=None,
+                      state: Optional[StateTuple] = None, eps: float = 1.0, return_state: bool = True,
+                      y_host: Optional[torch.Tensor] = None, pieces: Optional[int] = None,
+                      prologue: Optional[Prologue] = None):
+    """prefill() for inputs and output in host memory: q, k, v [B,H,L,D] on the CPU (pinned, or the
+    copies cannot overlap), y returned in `y_host` (pinned [B,H,L,D] of q's dtype; allocated pinned
+    if None).  The batch runs in `pieces` slices (default: one per batch row, at most 8): the
+    host->device copy of a slice, the kernels of the previous slice and the device->host copy of
+    the one before overlap, on two side streams and the current stream (PCIe carries both
+    directions at once).  The current stream's work after this call sees y_host complete; the
+    caller synchronises before reading it on the host.  `state` (on the device) and the returned
+    final state (on the device, unless return_state=False) are as in prefill().  Device staging
+    buffers for q, k, v, y are kept between calls (release_host_staging() frees them)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if q.is_cuda or k.is_cuda or v.is_cuda:
+        raise ValueError("prefill_from_host takes q, k, v in host memory; use prefill() for device tensors")
+    if q.dim() != 4:
+        raise ValueError(f"q must be [B,H,L,D]; got {tuple(q.shape)}")
+    B, H, L, D = q.shape
+    if y_host is None:
+        y_host = torch.empty(B, H, L, D, dtype=q.dtype, pin_memory=True)
+    elif tuple(y_host.shape) != (B, H, L, D) or y_host.is_cuda:
+        raise ValueError("y_host must be a host [B,H,L,D] tensor")
+    P = max(1, min(B, pieces if pieces is not None else min(B, 8)))
+    bounds = [B * i // P for i in range(P + 1)]
+    cur = torch.cuda.current_stream(dev)
+    h2d, d2h = _copy_stream_pair(dev)
+    qd, kd, vd, yd = _staging(dev, q, k, v, y_host.dtype)
+    lam, lam_sb = lambda_tensor(decay, B, H, dev)
+    h2d.wait_stream(cur)  # earlier work on the current stream (a previous call's kernels) is done with them
+    states = []
+    for i in range(P):
+        sl = slice(bounds[i], bounds[i + 1])
+        if sl.start == sl.stop:
+            continue
+        with torch.cuda.stream(h2d):
+            for dst, src in ((qd, q), (kd, k), (vd, v)):
+                dst[sl].copy_(src[sl], non_blocking=True)
+            landed = torch.cuda.Event()
+            landed.record(h2d)
+        cur.wait_event(landed)
+        lam_i = lam if lam_sb == 0 else lam.view(B, H)[sl]
+        st_i = None if state is None else tuple(t[sl] for t in state)
+        _, st = prefill(qd[sl], kd[sl], vd[sl], lam_i, state=st_i, eps=eps, return_state=return_state,
+                        y_out=yd[sl], prologue=prologue)
+        states.append(st)
+        done = torch.cuda.Event()
+        done.record(cur)
+        d2h.wait_event(done)
+        with torch.cuda.stream(d2h):
+            y_host[sl].copy_(yd[sl], non_blocking=True)
+    cur.wait_stream(d2h)  # later work on the current stream (a next call's kernels) follows the copies out
+    final = None
+    if return_state:
+        final = states[0] if len(states) == 1 else tuple(torch.cat(parts, dim=0) for parts in zip(*states))
+    return y_host, final
+
+
 def decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay, state: StateTuple,
                 eps: float = 1.0, inplace: bool = False, out_dtype: Optional[torch.dtype] = None,
                 y_out: Optional[torch.Tensor] = None, prologue: Optional[Prologue] = None):

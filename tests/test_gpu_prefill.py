@@ -146,3 +146,22 @@ def test_prefill_rejects_bad_input():
     q = torch.zeros(1, 2, 8, 64, device="cuda", dtype=torch.float16)
     with pytest.raises(TypeError):
         ops.prefill(q, q, q, 0.9)
+
+
+@pytest.mark.parametrize("pieces,per_row_decay,with_state", [(None, False, False), (2, True, True), (1, False, True)])
+def test_prefill_from_host_matches_device_prefill(pieces, per_row_decay, with_state):
+    """Host buffers in and out, the batch in slices whose copies overlap the kernels: same y and
+    final state as prefill() on device tensors."""
+    B, H, L, D = 3, 2, 300, 64
+    q, k, v = synth.make_qkv(B, H, L, D, seed=31, dtype=torch.bfloat16, device="cuda")
+    lam = (torch.rand(B, H) * 0.05 + 0.95) if per_row_decay else synth.make_lambdas(H, 0.99, 0.9999, seed=3)
+    st0 = synth.make_state(B, H, D, lam if not per_row_decay else lam[0], seed=4, t0=200, sigma=0.05,
+                           device="cuda") if with_state else None
+    y_ref, st_ref = ops.prefill(q, k, v, lam, state=st0)
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    y, st = ops.prefill_from_host(qh, kh, vh, lam, state=st0, pieces=pieces)
+    torch.cuda.synchronize()
+    assert not y.is_cuda
+    assert_close(y, cpu64(y_ref), TOL_BF16, "y")
+    for a, b in zip(st, st_ref):
+        assert_close(a, cpu64(b), TOL_BF16, "state")
