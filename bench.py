@@ -502,7 +502,7 @@ def bench_model(args, ws, rank, device, stream, peaks):
 
 
 SP = dict(B=1, H=16, D=128, L=1 << 20, lam=(0.999, 0.99995), seed=6)
-SP_FLOP_PER_TOKHEAD = 6 * 64 * 128 + 8 * 128 * 128   # SURVEY-style count at C = 64, D = 128: 180,224
+SP_FLOP_PER_TOKHEAD = 6 * 64 * 128 + 8 * 128 * 128   # the chunked form at C = 64, D = 128: 180,224 per token-head
 SP_BYTES_PER_TOKHEAD = 8 * 128                         # q, k, v in + y out, bf16
 
 
