@@ -161,8 +161,8 @@ PMA_API size_t pma_prefill_workspace_bytes(int B, int H, int L, int D, int dtype
  *   workspace   device scratch of at least pma_prefill_workspace_bytes(...).
  *
  * F32 inputs are computed with float32 arithmetic throughout (CUDA cores).
- * BF16 inputs with D = 64 run on tcgen05 tensor cores: bf16 operands, float32
- * accumulation, float32 state.  L == 0 copies state_in to state_out.
+ * BF16 inputs with D = 64 or D = 128 run on tcgen05 tensor cores: bf16 operands,
+ * float32 accumulation, float32 state.  L == 0 copies state_in to state_out.
  */
 PMA_API int pma_prefill(int B, int H, int L, int D,
                 const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
@@ -250,10 +250,11 @@ PMA_API size_t pma_prefill_ex_workspace_bytes(int B, int H, int L, int D, int dt
  * prologue NULL is the identity prologue (= pma_prefill).  workspace: at least
  * pma_prefill_ex_workspace_bytes(...).  Other arguments and results as pma_prefill;
  * PMA_ERR_ARGUMENT if kv_groups < 1 or does not divide H.
- * The CUDA-core kernels apply the prologue as they load rows.  The tensor-core kernel
- * applies the GQA map in its tensor-map coordinates and a bf16-exact q_scale in its prep
- * warps; LayerNorms (and a q_scale bf16 cannot hold) run first as one HBM pass that writes
- * the normalised rows into the workspace (128 bytes read + 128 written per row).
+ * The CUDA-core kernels apply the prologue as they load rows.  The tensor-core kernels
+ * apply the GQA map in their tensor-map coordinates and a bf16-exact q_scale as they stage
+ * q.  At D = 64, LayerNorms (and a q_scale bf16 cannot hold) run first as one HBM pass that
+ * writes the normalised rows into the workspace (128 bytes read + 128 written per row); at
+ * D = 128 such a prologue selects the CUDA-core kernel.
  */
 PMA_API int pma_prefill_ex(int B, int H, int L, int D,
                            const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
