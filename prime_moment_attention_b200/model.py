@@ -186,7 +186,8 @@ class DecodeGraph:
     """One greedy decode step of `model` for a fixed batch, captured in a CUDA graph.
 
     The per-layer states are owned here (copied from `states` once) and updated in place by
-    pma_decode_step_ex; `step()` replays the graph: token ids in `self.tokens` [B, 1] ->
+    pma_decode_step_ex (pma_selective_decode_step for selective layers, whose per-token decay is
+    computed inside the graph); `step()` replays the graph: token ids in `self.tokens` [B, 1] ->
     next greedy ids in `self.tokens` and the step's logits in `self.logits` [B, vocab].
     Mirrors the decode loop of generate (model.py:227-240) with temperature 0."""
 
@@ -220,8 +221,6 @@ class DecodeGraph:
         h = h[:, 0]  # [B, hidden]
         for layer, st, w_qkv, w_gu in zip(m.layers, self.states, self.w_qkv, self.w_gu):
             attn = layer.self_attn
-            if isinstance(attn, PrimeSelectiveMomentAttention):
-                raise NotImplementedError("DecodeGraph serves moment-attention layers; use generate() for selective")
             x = layer.input_layernorm(h)
             B = x.shape[0]
             H, D, Hk = attn.num_heads, attn.head_dim, attn.num_kv_heads
@@ -229,13 +228,21 @@ class DecodeGraph:
             q = qkv[:, :H * D].view(B, H, D)
             k = qkv[:, H * D:(H + Hk) * D].view(B, Hk, D)
             v = qkv[:, (H + Hk) * D:].view(B, Hk, D)
-            decay = getattr(attn, "decay_per_head", None)
-            decay = attn.decay if decay is None else decay
             pro = _prologue(attn)
             if pro is None:
                 raise NotImplementedError("DecodeGraph needs QK-norms the kernels fold (nn.LayerNorm over head_dim)")
-            y, _ = ops.decode_step(q, k, v, decay, st if write else tuple(t.clone() for t in st), eps=attn.eps,
-                                   inplace=True, prologue=pro)
+            st_step = st if write else tuple(t.clone() for t in st)
+            if isinstance(attn, PrimeSelectiveMomentAttention):
+                # this token's decay exp(-Delta / tau_h), Delta = clamp(softplus(delta_proj(x)), 1e-4, 50),
+                # and k scaled by beta_h, as in the step branch (selective.py:367-396)
+                delta = F.softplus(attn.delta_proj(x)).clamp(min=1e-4, max=50.0)  # [B, H]
+                log_decay = -delta.float() / attn.get_tau(x.device).view(1, H)
+                y, _ = ops.selective_decode_step(q, k, v, log_decay, attn.get_beta(x.device).float(), st_step,
+                                                 eps=attn.eps, inplace=True, prologue=pro)
+            else:
+                decay = getattr(attn, "decay_per_head", None)
+                decay = attn.decay if decay is None else decay
+                y, _ = ops.decode_step(q, k, v, decay, st_step, eps=attn.eps, inplace=True, prologue=pro)
             h = torch.addmm(h, y.reshape(B, H * D).to(h.dtype), attn.o_proj.weight.t())  # residual + o_proj
             gu = torch.mm(layer.post_attention_layernorm(h), w_gu.t())
             inter = gu.shape[1] // 2

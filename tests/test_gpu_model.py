@@ -63,3 +63,33 @@ def test_model_forward_and_generate_match_reference():
             toks.append(dg.step().clone())
     torch.cuda.synchronize()
     assert np.array_equal(torch.cat(toks, dim=1).cpu().numpy(), g["generated"][:, 12:])
+
+
+@pytest.mark.gpu
+def test_decode_graph_selective_layers_match_generate():
+    """A model with selective layers (per-token decay from delta_proj): the CUDA-graph decode step
+    gives the same greedy tokens as generate()."""
+    from prime_moment_attention_b200.model import DecodeGraph, PrimeConfig, PrimeForCausalLM
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(7)
+    cfg = PrimeConfig(vocab_size=97, hidden_size=64, num_layers=2, num_heads=4, head_dim=16, intermediate_size=96,
+                      decay=0.99, use_selective=True)
+    m = PrimeForCausalLM(cfg)
+    with torch.no_grad():  # leave the identity initialisation: data-dependent decays and temperatures
+        for layer in m.layers:
+            a = layer.self_attn
+            a.delta_proj.weight.normal_(0, 0.3)
+            a.log_tau.copy_(torch.log(torch.linspace(4.0, 400.0, 4)))
+            a.log_beta.copy_(torch.tensor([0.2, -0.1, 0.0, 0.3]))
+    m = m.cuda().eval()
+    ids = torch.randint(0, 97, (3, 10), generator=torch.Generator().manual_seed(8)).cuda()
+    with torch.inference_mode():
+        gen = m.generate(ids, max_new_tokens=6, temperature=0.0)
+        out = m(ids, return_states=True, last_logits_only=True)
+        first = torch.argmax(out["logits"][:, -1], dim=-1, keepdim=True)
+        dg = DecodeGraph(m, out["states"], first)
+        toks = [first.clone()]
+        for _ in range(5):
+            toks.append(dg.step().clone())
+    torch.cuda.synchronize()
+    assert np.array_equal(torch.cat(toks, dim=1).cpu().numpy(), gen[:, 10:].cpu().numpy())
