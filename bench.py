@@ -482,12 +482,12 @@ def bench_model(args, ws, rank, device, stream, peaks):
         dms = max_over_ranks(time_steps(dg.step, c["new_tokens"], 3, ws, device, stream), ws, device)
     # per token: 2 x the layer weights (the tied embedding / head is excluded: the head runs on the
     # last position only) + the moment core's chunked work per head and layer
-    # this package's launches: per layer and prefill step the QK-norm pass for q and for k, then the
-    # prefill (a state-only pass and the segment prefix too when the plan splits sequences); one
-    # decode-step kernel per layer in every replay of the decode graph
+    # this package's launches: per layer and prefill step the QK-norm pass for q and for k, the
+    # prefill (a state-only pass and the segment prefix too when the plan splits sequences) and the
+    # MLP's fused SwiGLU; per layer in every replay of the decode graph the decode step and SwiGLU
     from prime_moment_attention_b200 import _lib
     seg = _lib.load().pma_prefill_workspace_bytes(B, c["heads"], c["L"], c["head_dim"], _lib.PMA_BF16) > 256
-    launches_prefill = 3 * c["layers"] * (2 + (3 if seg else 1))
+    launches_prefill = 3 * c["layers"] * (2 + (3 if seg else 1) + 1)
     n_params = sum(p.numel() for n, p in m.named_parameters() if "embed" not in n)
     flop_tok = 2 * n_params + c["layers"] * c["heads"] * PREFILL_FLOP_PER_TOKHEAD
     tf = B * c["L"] * flop_tok / (ms * 1e-3) / 1e12
@@ -501,7 +501,7 @@ def bench_model(args, ws, rank, device, stream, peaks):
             "decode": {"metric": "model_decode_step_us", "value": round(dms * 1e3, 1), "unit": "us/step",
                        "tok_per_s": round(B * ws / (dms * 1e-3), 1), "steps": c["new_tokens"],
                        "path": "whole greedy step (embed, 12 layers, head, argmax) in one CUDA graph, states in place",
-                       "gpu_launches": c["new_tokens"] * c["layers"]},
+                       "gpu_launches": c["new_tokens"] * c["layers"] * 2},
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": tc_peak, "unit": "TFLOP/s",
                          "frac": round(tf / tc_peak, 4), "traffic": None, "peak_kind": peak_kind,
                          "flop_per_token": flop_tok},

@@ -381,6 +381,18 @@ PMA_API int pma_state_combine(int B, int H, int D, const float *lambda, int64_t 
                       int64_t len, const pma_state *T, const pma_state *P,
                       pma_stream_t stream);
 
+/*
+ * SwiGLU activation of the model's MLP in one pass: out = silu(gate) * up over
+ * rows x inter elements (PrimeMLP.forward, src/prime_moment_attention/model.py:59-68,
+ * where PyTorch runs silu and the product as two kernels).  Row strides are in
+ * elements (>= inter; the element axis is contiguous); dtype PMA_BF16 or PMA_F32 for
+ * all three arrays.  silu is computed in float32 and rounded to the storage type
+ * before the product, as the two-kernel sequence does, so results are identical.
+ */
+PMA_API int pma_swiglu(int64_t rows, int inter, const void *gate, int64_t gate_stride,
+                       const void *up, int64_t up_stride, void *out, int64_t out_stride,
+                       int dtype, pma_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -123,6 +123,9 @@ def load() -> ctypes.CDLL:
     L.pma_state_combine.argtypes = ([ctypes.c_int] * 3 + [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64]
                                     + [_P(State)] * 2 + [ctypes.c_void_p])
     L.pma_state_combine.restype = ctypes.c_int
+    L.pma_swiglu.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                             ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p]
+    L.pma_swiglu.restype = ctypes.c_int
     _lib = L
     return L
 

@@ -652,6 +652,21 @@ int pma_selective_decode_step(int N, int H, int D, const pma_seq_tensor *q, cons
                        stream, beta, true);
 }
 
+int pma_swiglu(int64_t rows, int inter, const void *gate, int64_t gate_stride, const void *up, int64_t up_stride,
+               void *out, int64_t out_stride, int dtype, pma_stream_t stream) {
+    if (rows < 0 || inter <= 0 || gate_stride < inter || up_stride < inter || out_stride < inter)
+        return PMA_ERR_ARGUMENT;
+    if (!supported_dtype(dtype)) return PMA_ERR_DTYPE;
+    if (rows == 0) return PMA_OK;
+    if (!gate || !up || !out) return PMA_ERR_ARGUMENT;
+    int rc;
+    DevInfo di;
+    if ((rc = device_info(&di))) return rc;
+    cudaError_t e = launch_swiglu(dtype, gate, gate_stride, up, up_stride, out, out_stride, rows, inter, di.sms,
+                                  reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? PMA_OK : cuda_fail(e);
+}
+
 int pma_state_combine(int B, int H, int D, const float *lambda, int64_t lambda_stride_b, int64_t len,
                       const pma_state *T, const pma_state *P, pma_stream_t stream) {
     if (B < 0 || H <= 0 || !lambda || lambda_stride_b < 0 || len < 0) return PMA_ERR_ARGUMENT;

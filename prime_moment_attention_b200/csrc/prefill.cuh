@@ -87,6 +87,10 @@ cudaError_t launch_state_combine(int B, int H, int D, const float *lambda, int64
 cudaError_t launch_qk_norm(const Seq &src, int B, int Hs, int L, const float *w, const float *b, float eps,
                            float scale, void *dst, int sms, cudaStream_t st);
 
+// silu(gate) * up over rows x inter elements (row strides in elements), bf16 or float32.
+cudaError_t launch_swiglu(int dtype, const void *g, int64_t gs, const void *u, int64_t us, void *o, int64_t os,
+                          int64_t rows, int inter, int sms, cudaStream_t st);
+
 // tcgen05 tensor-core prefill (bf16 inputs, D = 64).
 constexpr int TC_CHUNK = 128;
 bool tc_supported(int D, int idt);

@@ -66,7 +66,7 @@ class RMSNorm(nn.Module):
 
 
 class PrimeMLP(nn.Module):
-    """SwiGLU feed-forward (model.py:59-68)."""
+    """SwiGLU feed-forward (model.py:59-68); silu(gate) * up as one kernel (pma_swiglu)."""
 
     def __init__(self, hidden_size: int, intermediate_size: int):
         super().__init__()
@@ -75,7 +75,7 @@ class PrimeMLP(nn.Module):
         self.down_proj = nn.Linear(intermediate_size, hidden_size, bias=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+        return self.down_proj(ops.swiglu(self.gate_proj(x), self.up_proj(x)))
 
 
 class PrimeBlock(nn.Module):
@@ -246,7 +246,7 @@ class DecodeGraph:
             h = torch.addmm(h, y.reshape(B, H * D).to(h.dtype), attn.o_proj.weight.t())  # residual + o_proj
             gu = torch.mm(layer.post_attention_layernorm(h), w_gu.t())
             inter = gu.shape[1] // 2
-            h = torch.addmm(h, F.silu(gu[:, :inter]) * gu[:, inter:], layer.mlp.down_proj.weight.t())
+            h = torch.addmm(h, ops.swiglu(gu[:, :inter], gu[:, inter:]), layer.mlp.down_proj.weight.t())
         logits = m.lm_head(m.norm(h))
         nxt = torch.argmax(logits, dim=-1, keepdim=True)
         if write:

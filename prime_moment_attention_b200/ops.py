@@ -221,6 +221,26 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
     return y, st_out_t
 
 
+def swiglu(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """silu(gate) * up in one pass (pma_swiglu): gate and up [..., I] on the GPU (bf16 or float32, last
+    axis contiguous, leading axes flattenable to rows with one stride, e.g. column halves of one
+    [N, 2I] GEMM output).  Same values as F.silu(gate) * up."""
+    dev = _require_cuda(gate, up)
+    if gate.shape != up.shape or gate.dtype != up.dtype or gate.dtype not in _DT:
+        raise ValueError("gate and up must have one shape and a bf16 or float32 dtype")
+    I = gate.shape[-1]
+    g2, u2 = gate.reshape(-1, I), up.reshape(-1, I)  # views where the layout allows
+    if g2.stride(-1) != 1 or u2.stride(-1) != 1:
+        g2, u2 = g2.contiguous(), u2.contiguous()
+    if out is None:
+        out = torch.empty(gate.shape, dtype=gate.dtype, device=dev)
+    o2 = out.view(-1, I)
+    rc = _lib.load().pma_swiglu(g2.shape[0], I, g2.data_ptr(), g2.stride(0), u2.data_ptr(), u2.stride(0),
+                                o2.data_ptr(), o2.stride(0), _DT[gate.dtype], _stream(dev))
+    _lib.check("pma_swiglu", rc)
+    return out
+
+
 _copy_streams = {}
 _host_staging = {}  # device index -> (key, (q, k, v, y) device staging buffers)
 

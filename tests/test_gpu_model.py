@@ -93,3 +93,23 @@ def test_decode_graph_selective_layers_match_generate():
             toks.append(dg.step().clone())
     torch.cuda.synchronize()
     assert np.array_equal(torch.cat(toks, dim=1).cpu().numpy(), gen[:, 10:].cpu().numpy())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape,halves", [((5, 3072), True), ((2, 7, 96), False), ((3, 13), False)])
+def test_swiglu_matches_the_two_torch_kernels(dtype, shape, halves):
+    """pma_swiglu against F.silu(gate) * up, element for element: contiguous inputs, the column halves
+    of one [N, 2I] GEMM output (the decode graph's layout), and a width the 16-byte path cannot take."""
+    from prime_moment_attention_b200 import ops
+    gen = torch.Generator().manual_seed(sum(shape))
+    if halves:
+        gu = (torch.randn(shape[0], 2 * shape[1], generator=gen) * 3).to("cuda", dtype)
+        gate, up = gu[:, :shape[1]], gu[:, shape[1]:]
+    else:
+        gate = (torch.randn(*shape, generator=gen) * 3).to("cuda", dtype)
+        up = (torch.randn(*shape, generator=gen) * 3).to("cuda", dtype)
+    ref = torch.nn.functional.silu(gate) * up
+    out = ops.swiglu(gate, up)
+    torch.cuda.synchronize()
+    assert out.shape == ref.shape and torch.equal(out, ref)
