@@ -193,3 +193,16 @@ def test_selective_module_parameters_and_identity_init():
     lam = torch.exp(-delta / m.get_tau(torch.device("cpu")))
     assert torch.allclose(lam, torch.full_like(lam, 0.99), atol=1e-6)
     assert torch.all(m.get_beta(torch.device("cpu")) == 1.0)
+
+
+def test_new_entries_refuse_cpu_tensors():
+    """The fused SwiGLU runs on CUDA tensors only (no CPU fallback); the host-buffer prefill takes
+    host tensors and refuses device ones."""
+    from prime_moment_attention_b200 import ops
+    x = torch.ones(2, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.swiglu(x, x)
+    if torch.cuda.is_available():
+        q = torch.zeros(1, 1, 4, 64, device="cuda")
+        with pytest.raises(ValueError, match="host memory"):
+            ops.prefill_from_host(q, q, q, 0.99)
