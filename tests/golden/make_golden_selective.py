@@ -85,8 +85,11 @@ def state_dict(prefix, st):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-src", default=os.environ.get("PRIME_REF_SRC", "/root/reference/src"))
+    ap.add_argument("--ref-src", default=os.environ.get("PRIME_REF_SRC"),
+                    help="the reference project's src/ directory (default: $PRIME_REF_SRC)")
     args = ap.parse_args()
+    if not args.ref_src:
+        ap.error("pass --ref-src <reference>/src or set PRIME_REF_SRC")
     sys.path.insert(0, args.ref_src)
     sys.dont_write_bytecode = True
     from prime_moment_attention.selective import PrimeSelectiveMomentAttention as Attn

@@ -117,3 +117,41 @@ def test_tc_config2_full_size():
     assert_close(y, cpu64(y32), TOL_BF16, "y vs fp32 kernel")
     for a, b_ in zip(st, st32):
         assert_close(a, cpu64(b_), TOL_BF16, "state vs fp32 kernel")
+
+
+def test_tc128_config5_law_long():
+    """Config 5's head shape and decay law (H=16, D=128, bf16, lambda log-U[0.999, 0.99995]) at
+    L = 2^16 through pma_prefill's segmented tensor-core path (state-only pass, segment prefix,
+    full pass): four sampled head-states against the float64 oracle over all tokens (y and every
+    final-state component), and every head-state against the float32 CUDA-core kernel run on the
+    same bf16-valued inputs.  Decays this close to 1 keep 2^16 tokens of history in the state, so
+    this is where bf16 carry operands would accumulate error.  The carry replaces the reference's
+    inter-chunk matmul (src/prime_moment_attention/chunked_ssd.py:113-126)."""
+    from concurrent.futures import ThreadPoolExecutor
+    c = synth.CONFIG5
+    B, H, L, D = c["B"], c["H"], 1 << 16, c["D"]
+    assert _lib.load().pma_prefill_workspace_bytes(B, H, L, D, _lib.PMA_BF16) > 256  # segmented plan
+    q, k, v = synth.make_qkv(B, H, L, D, seed=c["seed"], dtype=torch.bfloat16, device="cuda")
+    lam = synth.make_lambdas(H, *c["lam"], seed=c["seed"])
+    y, st = ops.prefill(q, k, v, lam, out_dtype=torch.float32, check=True)
+    heads = [int(torch.argmax(lam)), int(torch.argmin(lam)), 5, 11]
+    qc, kc, vc = q.cpu(), k.cpu(), v.cpu()
+    lam64 = lam_np(lam)
+
+    def ref(h):  # ctypes releases the GIL: the four oracle runs overlap
+        return O.prefill(qc[:, h:h + 1], kc[:, h:h + 1], vc[:, h:h + 1], lam64[h:h + 1])
+
+    with ThreadPoolExecutor(4) as ex:
+        refs = list(ex.map(ref, heads))
+    for h, (y_ref, st_ref) in zip(heads, refs):
+        ey = assert_close(y[:, h:h + 1], y_ref, TOL_BF16, f"y[h={h}]")
+        es = assert_state_close(tuple(s[:, h:h + 1] for s in st), st_ref, TOL_BF16, f"state[h={h}]")
+        print(f"config-5 law, L=2^16, head {h} (lambda={lam64[h]:.6f}): y {ey:.2e}, state "
+              + " ".join(f"{e:.2e}" for e in es))
+    y32, st32 = ops.prefill(q.float(), k.float(), v.float(), lam, out_dtype=torch.float32)
+    e = assert_close(y, cpu64(y32), TOL_BF16, "y vs fp32 kernel")
+    es = [assert_close(a, cpu64(b_), TOL_BF16, "state vs fp32 kernel") for a, b_ in zip(st, st32)]
+    print(f"config-5 law, L=2^16, all heads vs fp32 kernel: y {e:.2e}, state " + " ".join(f"{x:.2e}" for x in es))
+    _, st_only = ops.prefill(q, k, v, lam, want_y=False, check=True)
+    for a, b_ in zip(st_only, st32):
+        assert_close(a, cpu64(b_), TOL_BF16, "state-only call vs fp32 kernel")

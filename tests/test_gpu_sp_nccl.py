@@ -65,3 +65,49 @@ def test_sequence_parallel_prefill_nccl(D, dtype_name, tol):
                        join=True)
     assert len(out) == world
     assert max(out.values()) <= tol, dict(out)
+
+
+def _worker_config5(rank, world, port, out):
+    """Config 5's head shape and decay law at L = 2^16 in `world` equal shards: two sampled
+    head-states against the float64 oracle, every head-state against the float32 CUDA-core
+    kernel over the whole sequence on this rank's GPU."""
+    import torch.distributed as dist
+    from oracle import oracle as O
+    from prime_moment_attention_b200 import ops, sp, synth
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        c = synth.CONFIG5
+        B, H, L, D = c["B"], c["H"], 1 << 16, c["D"]
+        Ls = L // world
+        q, k, v = synth.make_qkv(B, H, L, D, seed=c["seed"], dtype=torch.bfloat16, device=dev)
+        lam = synth.make_lambdas(H, *c["lam"], seed=c["seed"])
+        sl = slice(rank * Ls, (rank + 1) * Ls)
+        y, final = sp.sequence_parallel_prefill(q[:, :, sl].contiguous(), k[:, :, sl].contiguous(),
+                                                v[:, :, sl].contiguous(), lam.to(dev), broadcast_final=True)
+        y32, st32 = ops.prefill(q.float(), k.float(), v.float(), lam.to(dev), out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        errs = [O.rel_err(y.double().cpu().numpy(), y32[:, :, sl].double().cpu().numpy())]
+        errs += [O.rel_err(f.double().cpu().numpy(), r.double().cpu().numpy()) for f, r in zip(final, st32)]
+        h = [int(torch.argmax(lam)), 7][rank % 2]
+        y_ref, s_ref = O.prefill(q[:, h:h + 1].cpu(), k[:, h:h + 1].cpu(), v[:, h:h + 1].cpu(),
+                                 lam.double().numpy()[h:h + 1])
+        errs.append(O.rel_err(y[:, h:h + 1].double().cpu().numpy(), y_ref[:, :, sl]))
+        errs += [O.rel_err(f[:, h:h + 1].double().cpu().numpy().reshape(r.shape), r) for f, r in zip(final, s_ref)]
+        out[rank] = max(errs)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sequence_parallel_config5_law_nccl():
+    world = 2
+    out = mp.Manager().dict()
+    mp.start_processes(_worker_config5, args=(world, _free_port(), out), nprocs=world, start_method="spawn",
+                       join=True)
+    assert len(out) == world
+    print(f"config-5 law, L=2^16 over {world} NCCL shards: max relative error per rank {dict(out)}")
+    assert max(out.values()) <= TOL_BF16, dict(out)
