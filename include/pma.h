@@ -21,9 +21,16 @@
  *     launched on `stream` (NULL = the legacy default stream) and run
  *     asynchronously; PMA_ERR_CUDA reports a launch failure.
  *   - No entry point allocates device memory.  Scratch space is passed in
- *     (pma_prefill_workspace_bytes says how much).
- *   - Entry points are re-entrant and hold no global mutable state other than a
- *     per-device cache of kernel attributes set once.
+ *     (pma_prefill_workspace_bytes says how much), except for
+ *     pma_prefill_no_alloc, whose scratch is a static device buffer.
+ *   - Entry points are re-entrant.  Global mutable state: a per-device cache of
+ *     kernel attributes set once; the fault word registered with
+ *     pma_set_fault_word (and the test hook pma_test_expire_waits); and the
+ *     static scratch buffer of pma_prefill_no_alloc with its per-device,
+ *     per-context cache of the buffer's address.
+ *   - Kernels that wait (the tensor-core prefills) bound every wait; a wait that
+ *     expires stops the launch early with unwritten outputs and records a nonzero
+ *     code in the workspace status word and in the registered fault word.
  *   - Sequence tensors (q, k, v, y) are [B, H, L, D] with arbitrary element
  *     strides on B, H, L and a contiguous D axis, so both the reference's
  *     [B,H,L,D] tensors and its transposed views of [B,L,H,D] projections
@@ -41,7 +48,7 @@
 extern "C" {
 #endif
 
-#define PMA_ABI_VERSION 2
+#define PMA_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define PMA_API __attribute__((visibility("default")))
@@ -125,6 +132,27 @@ PMA_API const char *pma_status_string(int status);
 PMA_API int pma_last_cuda_error(void);
 PMA_API const char *pma_cuda_error_string(int cuda_error);
 
+/*
+ * Registers `word`, a device-accessible int (device memory, or pinned host memory,
+ * which the host can read at any time without synchronising), as the process-wide
+ * fault word: every later launch of a kernel with bounded waits (the tensor-core
+ * prefills: pma_prefill, pma_prefill_ex, pma_prefill_no_alloc, pma_selective_prefill,
+ * pma_delta_prefill) stores the code of the first wait that expires into it when it
+ * still reads 0.  The library never clears it; NULL unregisters.  No counterpart in
+ * the reference, which has no device waits (its only failure signals are NaN checks,
+ * c/main.c:92-98 and model.py:221,228).
+ */
+PMA_API void pma_set_fault_word(int *word);
+
+/*
+ * Test hook for the failure path: with limit_ns > 0, every later tensor-core prefill
+ * launch first waits, with that bound, for a barrier phase that nothing completes;
+ * the wait expires before any copy or GEMM is issued, the launch records code 90
+ * (workspace status word and fault word) and returns without writing outputs.
+ * 0 restores normal operation.  For tests only; no counterpart in the reference.
+ */
+PMA_API void pma_test_expire_waits(unsigned long long limit_ns);
+
 /* Floats in one head-state: 2*D*D + 3*D + 1 (c/prime_moment.h:17 states the
  * same count for the reference's C runtime). */
 PMA_API size_t pma_state_floats(int D);
@@ -183,9 +211,13 @@ PMA_API int pma_prefill(int B, int H, int L, int D,
  * problems whose plan needs more (pma_prefill_workspace_bytes > 16 MiB: float32
  * or D = 128 with few head-states and long sequences) return PMA_ERR_WORKSPACE.
  * The first call on a device looks up the buffer's device address; make it
- * before any stream capture.  All calls on a device share the buffer: calls that
- * overlap on the GPU race and must be serialised by the caller.  Allocates
- * nothing.
+ * before any stream capture.  The address is kept per device together with the
+ * CUDA context that was current, and looked up again when another context is
+ * current; it does not survive a cudaDeviceReset of the device.  All calls on a
+ * device share the buffer: calls that overlap on the GPU race and must be
+ * serialised by the caller.  The buffer holds the status word, out of the
+ * caller's reach: register a fault word (pma_set_fault_word) to see an expired
+ * wait.  Allocates nothing.
  */
 PMA_API int pma_prefill_no_alloc(int B, int H, int L, int D,
                                  const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,

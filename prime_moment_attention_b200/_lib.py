@@ -72,6 +72,10 @@ def load() -> ctypes.CDLL:
     L.pma_status_string.argtypes = [ctypes.c_int]
     L.pma_status_string.restype = ctypes.c_char_p
     L.pma_last_cuda_error.restype = ctypes.c_int
+    L.pma_set_fault_word.argtypes = [ctypes.c_void_p]
+    L.pma_set_fault_word.restype = None
+    L.pma_test_expire_waits.argtypes = [ctypes.c_ulonglong]
+    L.pma_test_expire_waits.restype = None
     L.pma_cuda_error_string.argtypes = [ctypes.c_int]
     L.pma_cuda_error_string.restype = ctypes.c_char_p
     L.pma_state_floats.argtypes = [ctypes.c_int]

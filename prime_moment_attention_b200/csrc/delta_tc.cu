@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
     const float *alpha_g = p.alpha ? p.alpha + (size_t)bh * p.L : nullptr;
     TO *yb = want_y ? reinterpret_cast<TO *>(p.y.p) + b * p.y.sb + h * p.y.sh : nullptr;
     const float r2 = 0.70710678118654752f;
-    Ctl ctl{abort_flag, nullptr};
+    Ctl ctl{abort_flag, nullptr, p.fault};
 
     // ---- set-up: barrier, tensor memory, zero operand rows, the state
     if (tid == 0) {

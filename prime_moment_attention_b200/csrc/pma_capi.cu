@@ -1,5 +1,6 @@
 // pma_capi.cu -- the extern "C" entry points declared in include/pma.h:
 // argument validation on the host, planning (kernel, chunk, segments) and launch.
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -17,11 +18,20 @@ struct DevInfo {
 
 thread_local int g_last_cuda_error = 0;
 
-// PMA_ERR_CUDA with the cause remembered for pma_last_cuda_error().
-int cuda_fail(cudaError_t e) {
+// The caller's fault word (pma_set_fault_word) and the test hook's wait limit
+// (pma_test_expire_waits): read by every launch of a kernel with bounded waits.
+std::atomic<int *> g_fault_word{nullptr};
+std::atomic<unsigned long long> g_test_wait_ns{0};
+
+}  // namespace
+
+// PMA_ERR_CUDA with the cause remembered for pma_last_cuda_error() (also used by prefill_static.cu).
+int pma::cuda_fail(cudaError_t e) {
     g_last_cuda_error = (int)e;
     return PMA_ERR_CUDA;
 }
+
+namespace {
 
 inline int d_ok(const DevInfo &d) { return d.major == 10 ? PMA_OK : PMA_ERR_DEVICE; }
 
@@ -256,6 +266,10 @@ const char *pma_status_string(int status) {
 
 int pma_last_cuda_error(void) { return g_last_cuda_error; }
 
+void pma_set_fault_word(int *word) { g_fault_word.store(word); }
+
+void pma_test_expire_waits(unsigned long long limit_ns) { g_test_wait_ns.store(limit_ns); }
+
 const char *pma_cuda_error_string(int cuda_error) { return cudaGetErrorString((cudaError_t)cuda_error); }
 
 size_t pma_state_floats(int D) { return D > 0 ? state_floats(D) : 0; }
@@ -392,6 +406,8 @@ int prefill_impl(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_
     p.lam_sb = lambda_stride_b;
     p.eps = eps;
     p.status = nullptr;
+    p.fault = g_fault_word.load();
+    p.test_wait_ns = g_test_wait_ns.load();
 
     if (pl.ws_bytes) {  // clear the status word the tensor-core kernel reports timeouts in
         p.status = reinterpret_cast<int *>(workspace);
@@ -518,6 +534,7 @@ int pma_delta_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const
     p.norm_eps = norm_eps;
     p.state_in = state_in;
     p.state_out = state_out;
+    p.fault = g_fault_word.load();
     cudaError_t e = delta_tc_supported(D, chunk, q->dtype)
                         ? launch_delta_prefill_tc(p, y ? y->dtype : PMA_F32, st)
                         : launch_delta_prefill(p, D, chunk, q->dtype, y ? y->dtype : PMA_F32, st);
@@ -626,6 +643,8 @@ int pma_selective_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, c
     p.eps = eps;
     p.state_only = 0;
     p.status = nullptr;
+    p.fault = g_fault_word.load();
+    p.test_wait_ns = g_test_wait_ns.load();
     p.logdecay = log_decay;
     p.k_head_scale = beta;
     p.half_sq = 1;

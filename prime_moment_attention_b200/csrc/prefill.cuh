@@ -21,6 +21,8 @@ struct PrefillParams {
     float eps;
     int state_only;       // 1: skip the readout, start every segment from zero, write its state to `out`
     int *status;          // device status word (0 = ok); bounded waits record a code here
+    int *fault;           // registered fault word (pma_set_fault_word) or nullptr: expired waits record a code
+    unsigned long long test_wait_ns;  // test hook (pma_test_expire_waits): nonzero makes one wait expire
     // selective variant (CUDA-core kernel only, one segment):
     const float *logdecay;      // [B*H*L] log lambda_t per token, or nullptr (lambda per head)
     const float *k_head_scale;  // [H] k multiplied by it (the temperature beta_h), or nullptr
@@ -29,6 +31,9 @@ struct PrefillParams {
 
 // Workspace layout: [header: 256 B, int status word first][per-segment states, float32].
 constexpr size_t WS_HEADER = 256;
+
+// PMA_ERR_CUDA, with `e` recorded for pma_last_cuda_error() on the calling thread.
+int cuda_fail(cudaError_t e);
 
 struct DecodeParams {
     int N, H;
@@ -58,6 +63,7 @@ struct DeltaParams {
     float bound, norm_eps;
     const float *state_in;    // [B*H][D][2D] or nullptr (zero)
     float *state_out;         // [B*H][D][2D] or nullptr
+    int *fault;               // registered fault word or nullptr (tensor-core kernel's expired waits)
 };
 struct DeltaStepParams {
     int N, H;

@@ -14,12 +14,19 @@
 // loads the library holds one copy until the process exits.  Host code cannot
 // use the array's name as a device address, so the first call on each device
 // (with that device current) looks the address up with cudaGetSymbolAddress and
-// keeps it; make that first call before any stream capture.  All calls on a
-// device share the one buffer and it keeps the previous call's contents: the
-// status word is cleared by every call, and segment states are written before
-// they are read, so nothing else needs clearing; but calls that overlap on the
-// GPU (other streams, other host threads) race on it and must be serialised by
-// the caller.
+// keeps it; make that first call before any stream capture.  The address belongs
+// to the CUDA context the library's module is loaded into, so it is kept together
+// with that context and looked up again when a call finds another context current
+// (a host application that creates or switches contexts).  All calls on a device
+// share the one buffer and it keeps the previous call's contents: the status word
+// is cleared by every call, and segment states are written before they are read,
+// so nothing else needs clearing; but calls that overlap on the GPU (other
+// streams, other host threads) race on it and must be serialised by the caller.
+// The status word sits inside the buffer, out of the caller's reach; a caller
+// sees an expired wait through the fault word it registers with
+// pma_set_fault_word, which every launch of this entry point also writes.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "prefill.cuh"
@@ -30,8 +37,28 @@ constexpr size_t kScratchBytes = size_t(16) << 20;  // 16 MiB per device
 static __device__ __align__(256) unsigned char g_prefill_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
-void *g_scratch_addr[kMaxDevices];
+struct ScratchAddr {
+    CUcontext ctx;  // context the address was looked up in
+    void *ptr;
+};
+ScratchAddr g_scratch_addr[kMaxDevices];
 std::mutex g_scratch_mu;
+
+typedef CUresult (*CtxGetCurrent)(CUcontext *);
+
+// The driver's cuCtxGetCurrent, fetched through the runtime (the library does not link libcuda).
+CtxGetCurrent ctx_get_current() {
+    static CtxGetCurrent fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrent>(ptr);
+    });
+    return fn;
+}
 
 }  // namespace
 
@@ -40,17 +67,25 @@ extern "C" int pma_prefill_no_alloc(int B, int H, int L, int D, const pma_seq_te
                                     const pma_state *state_in, const pma_state *state_out, float eps,
                                     const pma_seq_tensor *y, pma_stream_t stream) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return PMA_ERR_CUDA;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return pma::cuda_fail(e);
     if (dev < 0 || dev >= kMaxDevices) return PMA_ERR_DEVICE;
     void *scratch = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_scratch_mu);
-        if (!g_scratch_addr[dev]) {
+        ScratchAddr &slot = g_scratch_addr[dev];
+        CUcontext ctx = nullptr;
+        const CtxGetCurrent get_ctx = ctx_get_current();
+        if (get_ctx && get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+        if (!slot.ptr || (ctx && ctx != slot.ctx)) {
             void *ptr = nullptr;
-            if (cudaGetSymbolAddress(&ptr, g_prefill_scratch) != cudaSuccess || !ptr) return PMA_ERR_CUDA;
-            g_scratch_addr[dev] = ptr;
+            if ((e = cudaGetSymbolAddress(&ptr, g_prefill_scratch)) != cudaSuccess) return pma::cuda_fail(e);
+            if (!ptr) return pma::cuda_fail(cudaErrorInvalidSymbol);
+            if (!ctx && get_ctx) get_ctx(&ctx);  // the lookup made the primary context current
+            slot.ctx = ctx;
+            slot.ptr = ptr;
         }
-        scratch = g_scratch_addr[dev];
+        scratch = slot.ptr;
     }
     if (!q) return PMA_ERR_ARGUMENT;
     // Same plan as pma_prefill; reject problems whose scratch exceeds the fixed buffer.

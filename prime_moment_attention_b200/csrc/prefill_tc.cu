@@ -85,7 +85,7 @@ enum {
     B_FULL0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_PREP0, B_PREP1, B_PREP2,
     B_IFULL0, B_IFULL1, B_PREADY0, B_PREADY1, B_DSFULL0, B_DSFULL1, B_DSFREE0, B_DSFREE1,
     B_QFREE0, B_QFREE1, B_CDONE0, B_CDONE1, B_SREADY0, B_SREADY1, B_OEMPTY, B_QEMPTY0, B_QEMPTY1, B_MLD0, B_MLD1, B_MLD2, B_MLD3,
-    B_FINAL, NBAR
+    B_FINAL, B_NEVER, NBAR
 };
 
 struct Small {
@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(512, 1)
     const int U = c_end - c_begin;
     const int n_last = min(C, p.L - (c_end - 1) * C);
     const float kbeta = (PT && p.k_head_scale) ? p.k_head_scale[h] : 1.f;
-    Ctl ctl{&sm.abort_flag, p.status};
+    Ctl ctl{&sm.abort_flag, p.status, p.fault};
 
     // ---- set-up: powers, barriers, tensor memory
     if (!PT && threadIdx.x <= C) sm.pw[threadIdx.x] = (float)pow((double)lam, (double)threadIdx.x);
@@ -247,8 +247,16 @@ __global__ void __launch_bounds__(512, 1)
     __syncthreads();
     const uint32_t tmem = sm.tmem_base;
     uint64_t *bar = sm.bar;
+    bool expired = false;  // test hook: a wait expired before any copy or GEMM was issued
+    if (p.test_wait_ns) {
+        if (threadIdx.x == 0) expire_test_wait(&bar[B_NEVER], ctl, p.test_wait_ns, 90);
+        __syncthreads();
+        expired = sm.abort_flag != 0;
+    }
 
-    if (warp == 0) {
+    if (expired) {
+        // nothing was issued: straight to the release of tensor memory
+    } else if (warp == 0) {
         // ============================== TMA producer
         if (lane == 0) {
             int issued = 0, fetched = 0;

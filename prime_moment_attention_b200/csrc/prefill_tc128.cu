@@ -80,7 +80,7 @@ constexpr uint32_t T_AT = 0, T_DS = 128, T_QQ = 256, T_ACC = 384, T_COLS = 512;
 constexpr int ISSUER = 384;             // lane 0 of warp 12 (quadrant 0, columns 96..127)
 
 // copies: q, k, v tiles; MMA groups (committed once per chunk each; M1B only drained on the way out)
-enum { B_FQ, B_FK, B_FV, B_M1, B_M1B, B_M2, B_M3, NBAR };
+enum { B_FQ, B_FK, B_FV, B_M1, B_M1B, B_M2, B_M3, B_NEVER, NBAR };
 
 struct Small {
     uint64_t bar[NBAR];
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(NT, 1)
     const int c_end = min(c_begin + seg_chunks, nchunks_total);
     const int U = max(c_end - c_begin, 0);
     const int n_last = U > 0 ? min(C, p.L - (c_end - 1) * C) : 0;
-    Ctl ctl{&sm.abort_flag, p.status};
+    Ctl ctl{&sm.abort_flag, p.status, p.fault};
     uint64_t *bar = sm.bar;
 
     // ---- set-up: powers, barriers, tensor memory, the incoming state
@@ -225,6 +225,12 @@ __global__ void __launch_bounds__(NT, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    bool expired = false;  // test hook: a wait expired before any copy or GEMM was issued
+    if (p.test_wait_ns) {
+        if (tid == 0) expire_test_wait(&bar[B_NEVER], ctl, p.test_wait_ns, 90);
+        __syncthreads();
+        expired = sm.abort_flag != 0;
+    }
     if (tid == 0) {
         float gs = 0.f;
         for (int j = 0; j <= C; ++j) {
@@ -272,7 +278,7 @@ __global__ void __launch_bounds__(NT, 1)
             }
         }
     };
-    if (tid == 0 && U > 0) {
+    if (tid == 0 && U > 0 && !expired) {
         prefetch_to(PREFETCH);
         const int t0 = c_begin * C;
         if (!SO) load_tile2(OFF_Q, &tq, &bar[B_FQ], t0, h);
@@ -281,7 +287,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     // phases of the four barriers, and which of them have an operation in flight
     uint32_t ph_q = 0, ph_k = 0, ph_v = 0;
-    bool pend_q = !SO && U > 0, pend_k = U > 0, pend_v = U > 0;
+    bool pend_q = !SO && U > 0 && !expired, pend_k = U > 0 && !expired, pend_v = U > 0 && !expired;
     int pend_m = -1;           // latest MMA commit not yet waited for (it covers every earlier MMA)
     uint32_t pend_par = 0;
     fence_proxy_async();  // the state tiles are read by the tensor core
@@ -319,7 +325,7 @@ __global__ void __launch_bounds__(NT, 1)
         }
     };
 
-    bool ok = true;
+    bool ok = !expired;
     for (int u = 0; u < U && ok; ++u) {
         const int n = (u == U - 1) ? n_last : C;
         const int par = u & 1;

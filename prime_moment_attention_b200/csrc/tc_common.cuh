@@ -59,12 +59,25 @@ __device__ __forceinline__ bool mbar_poll(uint64_t *b, uint32_t parity) {
 struct Ctl {
     volatile int *abort_flag;  // shared: any role gave up
     int *status;               // global: first failure code (nullable)
+    int *fault;                // the registered fault word (pma_set_fault_word; nullable): device
+                               // memory or pinned host memory, written with a plain store
 };
 
 __device__ __forceinline__ void give_up(const Ctl &ctl, int code) {
     *ctl.abort_flag = 1;
     if (ctl.status) atomicCAS(ctl.status, 0, code);
+    if (ctl.fault) {  // a plain store: pinned host memory need not support device atomics
+        volatile int *w = ctl.fault;
+        if (*w == 0) *w = code;
+        __threadfence_system();
+    }
 }
+
+// Test hook of the failure path: one thread waits for a barrier phase that nothing completes,
+// bounded by `limit_ns`, and gives up with `code` like any expired wait.  Runs before any copy or
+// GEMM is issued, so the CTA has nothing in flight when its roles see the abort flag.
+__device__ __forceinline__ void expire_test_wait(uint64_t *never, const Ctl &ctl, unsigned long long limit_ns,
+                                                 int code);
 
 __device__ __forceinline__ bool mbar_wait_slow(uint64_t *b, uint32_t parity, const Ctl &ctl, int code) {
     const unsigned long long t0 = gtimer();
@@ -83,6 +96,17 @@ __device__ __forceinline__ bool mbar_wait_slow(uint64_t *b, uint32_t parity, con
 __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, const Ctl &ctl, int code) {
     if (mbar_try(b, parity)) return true;
     return mbar_wait_slow(b, parity, ctl, code);
+}
+
+__device__ __forceinline__ void expire_test_wait(uint64_t *never, const Ctl &ctl, unsigned long long limit_ns,
+                                                 int code) {
+    const unsigned long long t0 = gtimer();
+    while (!mbar_try(never, 0)) {
+        if (gtimer() - t0 > limit_ns) {
+            give_up(ctl, code);
+            return;
+        }
+    }
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }

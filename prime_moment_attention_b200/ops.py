@@ -155,6 +155,50 @@ def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+class KernelFault(RuntimeError):
+    """A tensor-core prefill launch gave up: one of its bounded waits expired, so its outputs
+    were not written.  `code` identifies the wait."""
+
+    def __init__(self, code: int, where: str):
+        self.code = code
+        super().__init__(f"{where}: a tensor-core prefill launch recorded fault code {code} "
+                         "(a bounded wait expired; its outputs were not written)")
+
+
+_fault: Optional[torch.Tensor] = None  # pinned host int32 registered as the library's fault word
+_fault_view = None                     # numpy view of it: a plain memory read per check
+
+
+def _arm_faults() -> None:
+    """Register a pinned host word as the library's fault word (once per process).  Pinned host
+    memory from cudaHostAlloc is addressable by every device, and the host reads it without
+    synchronising, so a fault is seen by the next call on any device."""
+    global _fault, _fault_view
+    if _fault is None:
+        word = torch.zeros(1, dtype=torch.int32).pin_memory()
+        _lib.load().pma_set_fault_word(word.data_ptr())
+        _fault, _fault_view = word, word.numpy()
+
+
+def pending_fault() -> int:
+    """Code recorded by a finished tensor-core prefill launch since the last check (0 if none).
+    Does not synchronise: a launch still running has not reported yet."""
+    return int(_fault_view[0]) if _fault is not None else 0
+
+
+def check_faults(where: str = "prime_moment_attention_b200", synchronize: bool = False) -> None:
+    """Raise KernelFault (and clear the word) if a tensor-core prefill launch gave up.  Every
+    prefill entry of this module calls it before launching, so a fault surfaces at the next call
+    at the latest; synchronize=True first waits for the device's work."""
+    _arm_faults()
+    if synchronize:
+        torch.cuda.synchronize()
+    code = int(_fault_view[0])
+    if code:
+        _fault_view[0] = 0
+        raise KernelFault(code, where)
+
+
 def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
             state: Optional[StateTuple] = None, eps: float = 1.0, return_state: bool = True,
             out_dtype: Optional[torch.dtype] = None, y_out: Optional[torch.Tensor] = None,
@@ -163,11 +207,13 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
 
     Returns (y [B,H,L,D] or None, final state or None).  `y_out` may be a
     preallocated [B,H,L,D] view with any strides (e.g. a transpose of [B,L,H,D]).
-    `want_y=False` runs the state-only pass.  `check=True` synchronises and raises
-    if the kernel recorded a failure in its status word (a bounded wait expired).
+    `want_y=False` runs the state-only pass.  A tensor-core launch that gives up (a bounded wait
+    expired) raises KernelFault at the next prefill call of this module, or here with `check=True`,
+    which synchronises and reads the call's workspace status word and the fault word.
     With a `prologue`, q, k, v are the raw projections (k, v with H / kv_groups heads)
     and the kernels apply the GQA map, QK-norm and q scale as they load them."""
     dev = _require_cuda(q, k, v)
+    check_faults("prefill")
     if q.dim() != 4:
         raise ValueError(f"q must be [B,H,L,D]; got {tuple(q.shape)}")
     B, H, L, D = q.shape
@@ -214,10 +260,12 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
         rc = L_.pma_prefill_ex(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), ctypes.byref(pc),
                                lam.data_ptr(), lam_sb, st_in, st_out, float(eps), ys, wsp, ws_bytes, _stream(dev))
         _lib.check("pma_prefill_ex", rc)
-    if check and ws is not None:
-        code = int(ws[:4].view(torch.int32).item())
+    if check:
+        code = int(ws[:4].view(torch.int32).item()) if ws is not None else 0  # synchronises
         if code != 0:
-            raise RuntimeError(f"pma_prefill: kernel status word {code} (a bounded wait expired)")
+            _fault_view[0] = 0
+            raise KernelFault(code, "pma_prefill (workspace status word)")
+        check_faults("pma_prefill")
     return y, st_out_t
 
 
@@ -234,7 +282,15 @@ def swiglu(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = N
         g2, u2 = g2.contiguous(), u2.contiguous()
     if out is None:
         out = torch.empty(gate.shape, dtype=gate.dtype, device=dev)
-    o2 = out.view(-1, I)
+    elif (not isinstance(out, torch.Tensor) or tuple(out.shape) != tuple(gate.shape) or out.dtype != gate.dtype
+          or out.device != dev):
+        raise ValueError(f"out must be a {gate.dtype} tensor of shape {tuple(gate.shape)} on {dev}")
+    try:
+        o2 = out.view(-1, I)
+    except RuntimeError as e:
+        raise ValueError("out must flatten to [rows, I] rows of one stride") from e
+    if o2.stride(-1) != 1:
+        raise ValueError("out must have a contiguous last axis")
     rc = _lib.load().pma_swiglu(g2.shape[0], I, g2.data_ptr(), g2.stride(0), u2.data_ptr(), u2.stride(0),
                                 o2.data_ptr(), o2.stride(0), _DT[gate.dtype], _stream(dev))
     _lib.check("pma_swiglu", rc)
@@ -474,6 +530,7 @@ def delta_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch
     if k.dtype != q.dtype or v.dtype != q.dtype:
         raise TypeError("q, k, v must share one dtype")
     B, H, L, D = q.shape
+    check_faults("delta_prefill")
     L_ = _lib.load()
     qs, q = _seq(q)
     ks, k = _seq(k)
@@ -557,6 +614,7 @@ def selective_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, log_dec
         raise ValueError(f"k, v must be {kv_shape}")
     if k.dtype != q.dtype or v.dtype != q.dtype:
         raise TypeError("q, k, v must share one dtype")
+    check_faults("selective_prefill")
     L_ = _lib.load()
     qs, q = _seq(q)
     ks, k = _seq(k)

@@ -113,3 +113,22 @@ def test_swiglu_matches_the_two_torch_kernels(dtype, shape, halves):
     out = ops.swiglu(gate, up)
     torch.cuda.synchronize()
     assert out.shape == ref.shape and torch.equal(out, ref)
+
+
+@pytest.mark.gpu
+def test_swiglu_refuses_a_mismatched_out():
+    """A caller-supplied `out` must match gate in shape, dtype and device and have a contiguous last
+    axis; otherwise the kernel would write past it or store bf16 bits into float32."""
+    from prime_moment_attention_b200 import ops
+    gate = torch.randn(4, 96, device="cuda", dtype=torch.bfloat16)
+    up = torch.randn(4, 96, device="cuda", dtype=torch.bfloat16)
+    bad = [torch.empty(3, 96, device="cuda", dtype=torch.bfloat16),        # fewer rows
+           torch.empty(4, 96, device="cuda", dtype=torch.float32),         # another dtype
+           torch.empty(4, 96, dtype=torch.bfloat16),                       # host memory
+           torch.empty(96, 4, device="cuda", dtype=torch.bfloat16).t()]    # strided last axis
+    for out in bad:
+        with pytest.raises(ValueError):
+            ops.swiglu(gate, up, out=out)
+    out = torch.empty(4, 96, device="cuda", dtype=torch.bfloat16)
+    assert ops.swiglu(gate, up, out=out) is out
+    assert torch.equal(out, torch.nn.functional.silu(gate) * up)

@@ -69,3 +69,38 @@ def test_pool_rows_out_of_range_are_skipped():
     assert torch.all(y == 7.0)
     for a, b in zip(pool.state, before):
         assert torch.equal(a, b)
+
+
+def test_cache_decodes_in_place_on_pool_rows():
+    """PrimeMomentCache on StatePool rows: prefill states are set per layer, then every layer is
+    decoded in place through the cache (pma_decode_step_rows on the layer's rows) and through the
+    module's functional path (state in from get_state, new tuple back through set_state).  The
+    views the cache hands out keep pointing at the same rows, and y and the states match the
+    float64 oracle at the fp32 bar."""
+    from prime_moment_attention_b200 import PrimeMomentCache, ops, synth
+    B, H, D, layers = 3, 4, 64, 2
+    lam = synth.make_lambdas(H, 0.99, 0.9999, seed=12).cuda()
+    cache = PrimeMomentCache(num_layers=layers)
+    ref = {}
+    for layer in range(layers):
+        q, k, v = synth.make_qkv(B, H, 200 + layer, D, seed=50 + layer, device="cuda")
+        _, st = ops.prefill(q, k, v, lam)
+        cache.set_state(layer, st)
+        ref[layer] = O.prefill(q, k, v, lam.double().cpu().numpy())[1]
+    ptrs = {layer: [t.data_ptr() for t in cache.get_state(layer)] for layer in range(layers)}
+    for step in range(3):
+        for layer in range(layers):
+            q, k, v = synth.make_decode_tokens(B, H, D, seed=900 + 10 * step + layer, dtype=torch.float32,
+                                               device="cuda")
+            if step % 2 == 0:
+                y = cache.decode_step(layer, q, k, v, lam)
+            else:  # the module's functional step: fresh tensors, copied back into the rows
+                y, new = ops.decode_step(q, k, v, lam, cache.get_state(layer))
+                cache.set_state(layer, new)
+            y_ref, ref[layer] = O.decode_step(q, k, v, lam.double().cpu().numpy(), ref[layer])
+            assert O.rel_err(y.double().cpu().numpy(), y_ref) <= TOL_F32
+    for layer in range(layers):
+        got = cache.get_state(layer)
+        assert [t.data_ptr() for t in got] == ptrs[layer]
+        for g, r in zip(got, ref[layer]):
+            assert O.rel_err(g.double().cpu().numpy().reshape(r.shape), r) <= TOL_F32

@@ -77,3 +77,39 @@ def test_no_alloc_rejects_problems_beyond_its_buffer():
     rc = _entry()(B, H, L, D, ctypes.byref(_seq(q)), ctypes.byref(_seq(q)), ctypes.byref(_seq(q)), lam.data_ptr(), 0,
                   None, None, 1.0, ctypes.byref(_seq(y)), torch.cuda.current_stream().cuda_stream)
     assert rc == 5  # PMA_ERR_WORKSPACE
+
+
+def test_no_alloc_status_reaches_the_caller():
+    """The status word of this entry point lives in its static buffer, out of the caller's reach;
+    a caller sees an expired wait through the fault word it registers (pma_set_fault_word; here
+    the module's pinned host word).  Normal calls leave it 0; a launch made to give up by the
+    test hook (a bounded wait on a barrier nothing completes, before any work is issued) leaves
+    code 90, and the next normal call through this entry point is correct again."""
+    ops.check_faults(synchronize=True)  # registers the word; nothing pending
+    B, H, L, D = 2, 3, 300, 64
+    q, k, v = synth.make_qkv(B, H, L, D, seed=11, dtype=torch.bfloat16, device="cuda")
+    lam = synth.make_lambdas(H, 0.99, 0.9999, seed=11).cuda()
+    y_ref, _ = ops.prefill(q, k, v, lam, out_dtype=torch.float32)
+    f = _entry()
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call():
+        y = torch.full((B, H, L, D), float("nan"), device="cuda")
+        rc = f(B, H, L, D, ctypes.byref(_seq(q)), ctypes.byref(_seq(k)), ctypes.byref(_seq(v)), lam.data_ptr(), 0,
+               None, None, 1.0, ctypes.byref(_seq(y)), stream)
+        assert rc == 0, _lib.status_string(rc)
+        torch.cuda.synchronize()
+        return y
+
+    assert_close(call(), cpu64(y_ref), TOL_BF16, "y")
+    assert ops.pending_fault() == 0
+    _lib.load().pma_test_expire_waits(1_000_000)
+    try:
+        call()
+    finally:
+        _lib.load().pma_test_expire_waits(0)
+    assert ops.pending_fault() == 90
+    with pytest.raises(ops.KernelFault):
+        ops.check_faults()
+    assert_close(call(), cpu64(y_ref), TOL_BF16, "y after the expired wait")
+    assert ops.pending_fault() == 0
