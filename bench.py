@@ -38,9 +38,12 @@ sys.path.insert(0, HERE)
 PREFILL = dict(B=8, H=12, L=8192, D=64, lam=(0.99, 0.9999), seed=2)
 DECODE = dict(seqs=256, layers=12, H=12, D=64, lam=(0.99, 0.9999), t0=4096, sigma=0.01, seed=3, steps=1000)
 PREFILL_BYTES_PER_TOKHEAD = 8 * 64          # q,k,v in + y out, bf16: 8*D bytes
-# chunked form at C = 128 tokens, F = 2D = 128 moment features, per token-head:
+# algorithmic FLOPs per token-head: the dense-chunk count the reference executes at its chunk
+# C = 64 (chunked_ssd.py:90-93, 106-107, 146-148): 6*C*D + 8*D^2 = 57,344 (den/Z terms excluded)
+PREFILL_FLOP_PER_TOKHEAD = 6 * 64 * 64 + 8 * 64 * 64
+# what this kernel's chunked form issues at C = 128 tokens, F = 2D = 128 moment features:
 # scores 2*C*F + intra P.V 2*C*D + carry 2*F*D + state update 2*F*D = 81,920
-PREFILL_FLOP_PER_TOKHEAD = 2 * 128 * 128 + 2 * 128 * 64 + 2 * 128 * 64 + 2 * 128 * 64
+PREFILL_KERNEL_FLOP_PER_TOKHEAD = 2 * 128 * 128 + 2 * 128 * 64 + 2 * 128 * 64 + 2 * 128 * 64
 DECODE_BYTES_PER_HEADSTEP = 2 * (2 * 64 * 64 + 3 * 64 + 1) * 4 + 3 * 64 * 2 + 64 * 2  # 67,592
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of
 # each kernel on the bench workload; the commands and the rest of the numbers are in profiles/.
@@ -140,6 +143,16 @@ def barrier(ws):
         dist.barrier()
 
 
+def per_rank(x, ws: int):
+    """Every rank's value of x (a float or a small dict), in rank order; [x] with one rank."""
+    if ws == 1:
+        return [x]
+    import torch.distributed as dist
+    out = [None] * ws
+    dist.all_gather_object(out, x)
+    return out
+
+
 def max_over_ranks(x: float, ws: int, device) -> float:
     if ws == 1:
         return x
@@ -192,6 +205,96 @@ def cpu_decode_sample(target_s: float = 6.0):
     return {"value": us, "unit": "us/step", "cores": threads, "kind": "reference",
             "sample": f"reference c/prime_moment.c prime_step (additive, eps=1), {nstates} of {total_states} "
                       f"seq x layer states (12 heads each), 4 steps, {threads} threads, scaled to all states"}
+
+
+def _reference_package():
+    """The reference's PyTorch package as installed in baseline/_ref (pip install --target), or None."""
+    ref_dir = os.path.join(HERE, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "prime_moment_attention")):
+        return None
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    import prime_moment_attention
+    return prime_moment_attention
+
+
+def cpu_pytorch_prefill_sample(target_s: float = 10.0):
+    """The reference's PyTorch chunked prefill (chunked_prime_ssd_core, chunked_ssd.py:48-184) on all
+    host threads, at config 2's shapes and laws: per head slice (the reference holds one scalar decay
+    per call), bf16 q/k/v cast to float32 as the module does (attention.py:104-106), chunk 64,
+    eps 1, final state returned.  Times whole batch rows of 12 heads x 8192 tokens, as many as
+    fit ~target_s after a one-head calibration; tok/s = rows x 8192 / seconds."""
+    import torch
+    ref = _reference_package()
+    if ref is None:
+        return {"unavailable": "baseline/_ref holds no reference install"}
+    from prime_moment_attention.chunked_ssd import chunked_prime_ssd_core
+    from prime_moment_attention_b200 import synth
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    c = PREFILL
+    H, L, D = c["H"], c["L"], c["D"]
+    lam = synth.make_lambdas(H, *c["lam"], seed=c["seed"]).tolist()
+
+    def row(seed, heads):
+        q, k, v = synth.make_qkv(1, H, L, D, seed=seed, dtype=torch.bfloat16)
+        q, k, v = q.float(), k.float(), v.float()
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            for h in heads:
+                chunked_prime_ssd_core(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], decay=lam[h], eps=1.0,
+                                       chunk_size=64, return_state=True)
+        return time.perf_counter() - t0
+
+    row(1, [0])  # warm-up
+    per_head = row(2, [0])
+    rows = int(max(1, min(c["B"], target_s / max(per_head * H, 1e-6))))
+    dt = sum(row(10 + r, range(H)) for r in range(rows))
+    return {"value": round(rows * L / dt, 1), "unit": "tok/s", "cores": threads, "kind": "reference_pytorch",
+            "sample": f"reference chunked_prime_ssd_core (PyTorch, float32), {rows} of {c['B']} batch rows x "
+                      f"{H} heads (one call per head) x L={L}, D={D}, chunk 64, torch threads={threads}, "
+                      f"{dt:.1f} s"}
+
+
+def cpu_pytorch_decode_sample(target_s: float = 6.0):
+    """The reference's PyTorch decode branch (PrimeMomentAttention.forward with L == 1,
+    attention.py:77-143, projections and QK-norm included) on all host threads, at config 3's shape:
+    one layer = one module call on 256 sequences x 12 heads, D = 64, from a seeded state; the
+    reference module holds one scalar decay (0.9995 here).  Times whole layer steps, as many as fit
+    ~target_s, and scales to the 12 layers of a config-3 step: us per step."""
+    import torch
+    ref = _reference_package()
+    if ref is None:
+        return {"unavailable": "baseline/_ref holds no reference install"}
+    from prime_moment_attention.attention import PrimeMomentAttention
+    from prime_moment_attention_b200 import synth
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    dc = DECODE
+    N, H, D = dc["seqs"], dc["H"], dc["D"]
+    torch.manual_seed(dc["seed"])
+    m = PrimeMomentAttention(hidden_size=H * D, num_heads=H, head_dim=D, decay=0.9995, use_qk_norm=True).eval()
+    st = synth.make_state(N, H, D, torch.full((H,), 0.9995), seed=dc["seed"], t0=dc["t0"], sigma=dc["sigma"])
+    x = torch.randn(N, 1, H * D, generator=torch.Generator().manual_seed(dc["seed"]))
+
+    def layer_step(state):
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            _, state = m(x, state=state, return_state=True)
+        return time.perf_counter() - t0, state
+
+    _, st = layer_step(st)  # warm-up
+    dt, st = layer_step(st)
+    n = int(max(1, min(12, target_s / max(dt, 1e-6))))
+    tot = 0.0
+    for _ in range(n):
+        t, st = layer_step(st)
+        tot += t
+    us = tot / n * dc["layers"] * 1e6
+    return {"value": round(us, 1), "unit": "us/step", "cores": threads, "kind": "reference_pytorch",
+            "sample": f"reference PrimeMomentAttention.forward, L=1 (PyTorch, float32, projections and QK-norm "
+                      f"included), {N} seqs x {H} heads, D={D}, {n} layer steps timed, x{dc['layers']} layers, "
+                      f"torch threads={threads}"}
 
 
 def run_reference_arm(args):
@@ -268,18 +371,25 @@ def bench_prefill(args, ws, rank, device, stream, peaks):
     clocks.start()  # before the warm-up, so that the timed steps follow it back to back
     ms = time_steps(step, args.steps, args.warmup, ws, device, stream)
     clk = clocks.stop()
+    rank_ms = per_rank(round(ms, 5), ws)
+    rank_clk = per_rank(clk, ws)
     ms = max_over_ranks(ms, ws, device)
     tokens = B * L * ws
     tokheads = B * L * H
     algo_bytes = tokheads * PREFILL_BYTES_PER_TOKHEAD
     algo_flop = tokheads * PREFILL_FLOP_PER_TOKHEAD
+    kern_flop = tokheads * PREFILL_KERNEL_FLOP_PER_TOKHEAD
     bw = algo_bytes / (ms * 1e-3) / 1e9
     tf = algo_flop / (ms * 1e-3) / 1e12
+    tfk = kern_flop / (ms * 1e-3) / 1e12
     roof = {"bound": "hbm", "achieved": round(bw, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(bw / hbm_peak, 4),
             "traffic": PREFILL_TRAFFIC if (B, H, L, D) == (c["B"], c["H"], c["L"], c["D"]) else None,
             "peak_kind": peak_kind,
-            "tensor": {"achieved": round(tf, 1), "peak": tc_peak, "unit": "TFLOP/s", "frac": round(tf / tc_peak, 4)},
+            "tensor": {"achieved": round(tf, 1), "peak": tc_peak, "unit": "TFLOP/s", "frac": round(tf / tc_peak, 4),
+                       "flop_per_tokhead": PREFILL_FLOP_PER_TOKHEAD,
+                       "kernel_flop_per_tokhead": PREFILL_KERNEL_FLOP_PER_TOKHEAD,
+                       "kernel_achieved": round(tfk, 1), "kernel_frac": round(tfk / tc_peak, 4)},
             "timed": "whole pma_prefill call (all its launches), CUDA events on the launching stream",
             "algorithmic_bytes_per_launch": algo_bytes, "algorithmic_flop_per_launch": algo_flop}
 
@@ -305,7 +415,8 @@ def bench_prefill(args, ws, rank, device, stream, peaks):
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
                     "path": "pinned host q,k,v -> ops.prefill_from_host: per batch slice H2D, pma_prefill (C ABI), "
                             "D2H, the slices' copies and kernels overlapped on 3 streams -> pinned host y"},
-            "gpu_launches": args.steps * launches_per_step, "clocks": clk}
+            "gpu_launches": args.steps * launches_per_step, "clocks": clk,
+            **({"per_rank": {"ms_per_step": rank_ms, "clocks": rank_clk}} if ws > 1 else {})}
 
 
 def bench_decode(args, ws, rank, device, stream, peaks):
@@ -330,8 +441,10 @@ def bench_decode(args, ws, rank, device, stream, peaks):
     dclk = ClockSampler(device.index)
     dclk.start()
     dsteps = args.decode_steps or dc["steps"]
-    dms = max_over_ranks(time_steps(dstep, dsteps, max(3, args.warmup), ws, device, stream), ws, device)
+    dms = time_steps(dstep, dsteps, max(3, args.warmup), ws, device, stream)
     dclk_r = dclk.stop()
+    ranks = {"ms_per_step": per_rank(round(dms, 5), ws), "clocks": per_rank(dclk_r, ws)}
+    dms = max_over_ranks(dms, ws, device)
     d_bytes = N * HD * DECODE_BYTES_PER_HEADSTEP
     d_bw = d_bytes / (dms * 1e-3) / 1e9
     return {"metric": "decode_step_us", "value": round(dms * 1e3, 2), "unit": "us/step",
@@ -342,7 +455,7 @@ def bench_decode(args, ws, rank, device, stream, peaks):
             "roofline": {"bound": "hbm", "achieved": round(d_bw, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(d_bw / hbm_peak, 4), "traffic": DECODE_TRAFFIC, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": d_bytes},
-            "gpu_launches": dsteps, "clocks": dclk_r}
+            "gpu_launches": dsteps, "clocks": dclk_r, **({"per_rank": ranks} if ws > 1 else {})}
 
 
 def cpu_delta_sample(target_s: float = 8.0):
@@ -537,8 +650,10 @@ def bench_sp(args, ws, rank, device, stream, peaks):
     steps = max(3, min(args.steps, 5))
     clk = ClockSampler(device.index)
     clk.start()
-    ms = max_over_ranks(time_steps(step, steps, 3, ws, device, stream), ws, device)
+    ms = time_steps(step, steps, 3, ws, device, stream)
     clk_r = clk.stop()
+    ranks = {"ms_per_step": per_rank(round(ms, 5), ws), "clocks": per_rank(clk_r, ws)}
+    ms = max_over_ranks(ms, ws, device)
     tokheads = c["B"] * c["L"] * c["H"]
     tf = tokheads * SP_FLOP_PER_TOKHEAD / (ms * 1e-3) / 1e12
     bw = tokheads * SP_BYTES_PER_TOKHEAD / (ms * 1e-3) / 1e9
@@ -562,7 +677,7 @@ def bench_sp(args, ws, rank, device, stream, peaks):
                                     "frac": round(tf / (peaks[1] * ws), 4)},
                          "algorithmic_bytes_per_step": tokheads * SP_BYTES_PER_TOKHEAD,
                          "algorithmic_flop_per_step": tokheads * SP_FLOP_PER_TOKHEAD},
-            "gpu_launches": steps * per_step, "clocks": clk_r}
+            "gpu_launches": steps * per_step, "clocks": clk_r, **({"per_rank": ranks} if ws > 1 else {})}
 
 
 def bench_selective(args, ws, rank, device, stream, peaks):
@@ -640,6 +755,37 @@ def bench_selective(args, ws, rank, device, stream, peaks):
     return {"prefill": pre, "decode": dec}
 
 
+def _with_summary(line: dict) -> dict:
+    """The line with a compact `summary` of every part right after the headline keys, so that a
+    reader that keeps only the first keys or the head of the line sees all the numbers."""
+    s = {}
+
+    def put(key, part, frac=True):
+        if isinstance(part, dict) and "value" in part:
+            s[key] = part["value"]
+            if frac and isinstance(part.get("roofline"), dict):
+                s[key + "_frac"] = part["roofline"].get("frac")
+
+    put("prefill_ms", {"value": line.get("ms_per_step"), "roofline": line.get("roofline")})
+    put("e2e_tok_s", line.get("e2e"), frac=False)
+    put("decode_us", line.get("decode"))
+    for name in ("selective", "delta"):
+        part = line.get(name) or {}
+        put(f"{name}_prefill_ms", {"value": (part.get("prefill") or {}).get("ms_per_step"),
+                                   "roofline": (part.get("prefill") or {}).get("roofline")})
+        put(f"{name}_decode_us", part.get("decode"))
+    sp = line.get("sp") or {}
+    put("sp_ms", {"value": sp.get("ms_per_step"), "roofline": sp.get("roofline")})
+    md = line.get("model") or {}
+    put("model_prefill_ms", {"value": md.get("ms_per_step"), "roofline": md.get("roofline")})
+    put("model_decode_us", md.get("decode"), frac=False)
+    head = [k for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step") if k in line]
+    out = {k: line[k] for k in head}
+    out["summary"] = {k: v for k, v in s.items() if v is not None}
+    out.update({k: v for k, v in line.items() if k not in out})
+    return out
+
+
 def run_ours(args):
     import torch
     ws, rank, local = dist_setup()
@@ -697,13 +843,23 @@ def run_ours(args):
                 line["cpu_baseline"] = cpu_prefill_sample()
         except Exception as e:  # the baseline must not sink the GPU number
             line["cpu_baseline"] = {"error": str(e)[:200]}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        # the reference's PyTorch path timed on the same host cores, beside its C99 runtime
+        for key, fn, where in (("prefill", cpu_pytorch_prefill_sample, line),
+                               ("decode", cpu_pytorch_decode_sample, line.get("decode"))):
+            if where is None or (key == "prefill" and line.get("metric") != "prefill_tok_per_s"):
+                continue
+            try:
+                where["cpu_baseline_pytorch"] = fn()
+            except Exception as e:  # the baseline must not sink the GPU number
+                where["cpu_baseline_pytorch"] = {"error": str(e)[:200]}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and "delta" in line:
         try:
             line["delta"]["prefill"]["cpu_baseline"] = cpu_delta_sample()
         except Exception as e:
             line["delta"]["prefill"]["cpu_baseline"] = {"error": str(e)[:200]}
     if rank == 0:
-        print(json.dumps(line))
+        print(json.dumps(_with_summary(line)))
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -200,6 +200,27 @@ PMA_API int pma_prefill(int B, int H, int L, int D,
                 void *workspace, size_t workspace_bytes, pma_stream_t stream);
 
 /*
+ * Output pass of a two-pass prefill, for callers that learn the state entering a sequence only
+ * after they have its state from a zero start (sequence shards on several GPUs: every shard's
+ * zero-start state is exchanged before any shard can compute its outputs).  A state-only
+ * pma_prefill call (y = NULL, state_in = NULL) leaves in its workspace the state entering each
+ * of its segments from a zero start; given that same workspace, unchanged, and the same B, H, L,
+ * D, q, k, v, lambda and device, this call adds lambda^start * state_in to those states and runs
+ * the full pass from them, without repeating the state-only pass.  y is required; other arguments
+ * and results as pma_prefill.  When the plan has one segment per head-state the workspace holds
+ * no states and this is pma_prefill.
+ *
+ * Replaces the second of the two chunked_prime_ssd_core calls a sequence split over devices would
+ * need; the reference's own inter-chunk carry is the dense [nc x nc] matmul of chunked_ssd.py:113-126.
+ */
+PMA_API int pma_prefill_resume(int B, int H, int L, int D,
+                               const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
+                               const float *lambda, int64_t lambda_stride_b,
+                               const pma_state *state_in, const pma_state *state_out,
+                               float eps, const pma_seq_tensor *y,
+                               void *workspace, size_t workspace_bytes, pma_stream_t stream);
+
+/*
  * pma_prefill without a caller-provided workspace, for callers that cannot
  * allocate device memory (a plugin whose host application owns all device memory
  * through its own pool, FFI callers without a device allocator, loops where an

@@ -88,6 +88,8 @@ def load() -> ctypes.CDLL:
                               + [_P(State)] * 2 + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p,
                                                    ctypes.c_size_t, ctypes.c_void_p])
     L.pma_prefill.restype = ctypes.c_int
+    L.pma_prefill_resume.argtypes = L.pma_prefill.argtypes
+    L.pma_prefill_resume.restype = ctypes.c_int
     L.pma_decode_step.argtypes = ([ctypes.c_int] * 3 + [_P(SeqTensor)] * 3 + [ctypes.c_void_p, ctypes.c_int64]
                                   + [_P(State)] * 2 + [ctypes.c_float, _P(SeqTensor), ctypes.c_void_p])
     L.pma_decode_step.restype = ctypes.c_int

@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
     float *const red = reinterpret_cast<float *>(smem + OFF_RED);
     uint64_t *const bar = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_BAR + 8);
-    int *const abort_flag = reinterpret_cast<int *>(smem + OFF_BAR + 12);
+    CtlShared *const ctl_sh = reinterpret_cast<CtlShared *>(smem + OFF_BAR + 16);
     const uint32_t sb = su32(smem);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -97,12 +97,12 @@ __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
     const float *alpha_g = p.alpha ? p.alpha + (size_t)bh * p.L : nullptr;
     TO *yb = want_y ? reinterpret_cast<TO *>(p.y.p) + b * p.y.sb + h * p.y.sh : nullptr;
     const float r2 = 0.70710678118654752f;
-    Ctl ctl{abort_flag, nullptr, p.fault};
+    Ctl ctl{ctl_sh, nullptr};
 
     // ---- set-up: barrier, tensor memory, zero operand rows, the state
     if (tid == 0) {
         mbar_init(bar, 1);
-        *abort_flag = 0;
+        init_ctl(*ctl_sh, p.fault);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {

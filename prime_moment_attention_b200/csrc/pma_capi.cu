@@ -168,7 +168,8 @@ int prologue_of(const pma_prologue *pp, int H, Prologue *out) {
 int prefill_impl(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
                  const pma_seq_tensor *v, const pma_prologue *prologue, const float *lambda,
                  int64_t lambda_stride_b, const pma_state *state_in, const pma_state *state_out, float eps,
-                 const pma_seq_tensor *y, void *workspace, size_t workspace_bytes, pma_stream_t stream);
+                 const pma_seq_tensor *y, void *workspace, size_t workspace_bytes, pma_stream_t stream,
+                 bool resume = false);
 int decode_impl(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
                 const pma_prologue *prologue, const float *lambda, int64_t lambda_stride_n, const int32_t *rows,
                 int pool_rows, const pma_state *state_in, const pma_state *state_out, float eps,
@@ -314,6 +315,15 @@ int pma_prefill_ex(int B, int H, int L, int D, const pma_seq_tensor *q, const pm
                         workspace, workspace_bytes, stream);
 }
 
+int pma_prefill_resume(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
+                       const pma_seq_tensor *v, const float *lambda, int64_t lambda_stride_b,
+                       const pma_state *state_in, const pma_state *state_out, float eps, const pma_seq_tensor *y,
+                       void *workspace, size_t workspace_bytes, pma_stream_t stream) {
+    if (!y) return PMA_ERR_ARGUMENT;  // the output pass is what this entry runs
+    return prefill_impl(B, H, L, D, q, k, v, nullptr, lambda, lambda_stride_b, state_in, state_out, eps, y,
+                        workspace, workspace_bytes, stream, true);
+}
+
 int pma_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
                     const float *lambda, int64_t lambda_stride_n, const pma_state *state_in,
                     const pma_state *state_out, float eps, const pma_seq_tensor *y, pma_stream_t stream) {
@@ -345,7 +355,8 @@ namespace {
 int prefill_impl(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
                  const pma_seq_tensor *v, const pma_prologue *prologue, const float *lambda,
                  int64_t lambda_stride_b, const pma_state *state_in, const pma_state *state_out, float eps,
-                 const pma_seq_tensor *y, void *workspace, size_t workspace_bytes, pma_stream_t stream) {
+                 const pma_seq_tensor *y, void *workspace, size_t workspace_bytes, pma_stream_t stream,
+                 bool resume) {
     if (B < 0 || H <= 0 || L < 0 || !lambda || lambda_stride_b < 0) return PMA_ERR_ARGUMENT;
     if (!supported_d(D)) return PMA_ERR_HEAD_DIM;
     int rc;
@@ -422,6 +433,18 @@ int prefill_impl(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_
     }
 
     float *ws = reinterpret_cast<float *>(reinterpret_cast<char *>(workspace) + WS_HEADER);
+    if (resume) {
+        // the workspace holds the state entering every segment from a zero start (left there by a
+        // state-only call with the same plan): shift them to state_in, then the full pass
+        if (state_in && (e = launch_segment_resume(BH, H, D, pl.nseg, pl.seg_len, ws, user_ref(state_in), lambda,
+                                                   lambda_stride_b, st)) != cudaSuccess)
+            return cuda_fail(e);
+        p.in = packed_ref(ws, pl.nseg);
+        p.out = user_ref(state_out);
+        p.state_only = 0;
+        e = launch_prefill(pl, p, D, q->dtype, ydt, dim3(BH, pl.nseg), st);
+        return e == cudaSuccess ? PMA_OK : cuda_fail(e);
+    }
     // 1. each segment's own state from zero (the last one only when no y is wanted)
     PrefillParams ps = p;
     ps.y = SeqOut{nullptr, 0, 0, 0};

@@ -85,6 +85,9 @@ cudaError_t launch_prefill_simt(const PrefillParams &p, int D, int idt, int ydt,
 int simt_chunk(int D);
 cudaError_t launch_segment_prefix(int BH, int H, int D, int nseg, int seg_len, int L, float *ws, const StateRef &in,
                                   const StateRef &final_out, const float *lambda, int64_t lam_sb, cudaStream_t st);
+// ws[s] += l^(s * seg_len) * in for every segment s (in: user-layout states entering the sequence).
+cudaError_t launch_segment_resume(int BH, int H, int D, int nseg, int seg_len, float *ws, const StateRef &in,
+                                  const float *lambda, int64_t lam_sb, cudaStream_t st);
 cudaError_t launch_state_combine(int B, int H, int D, const float *lambda, int64_t lam_sb, int64_t len,
                                  const pma_state &T, const pma_state &P, cudaStream_t st);
 

@@ -64,6 +64,33 @@ __global__ void segment_prefix_kernel(int BH, int H, int D, int nseg, int seg_le
     if (final_out.present()) *comp(final_out.at(bh, 0, D)) = P;
 }
 
+// ws[s] += l^(s * seg_len) * P_in: the states entering the segments, left in the workspace by a
+// state-only call from a zero start (segment_prefix_kernel), shifted to the incoming state P_in.
+// Every component of the recurrence decays by l per token, so a start state P_in adds l^t P_in
+// to the state after t tokens.
+__global__ void segment_resume_kernel(int BH, int H, int D, int nseg, int seg_len, float *ws, StateRef in,
+                                      const float *lambda, int64_t lam_sb) {
+    const size_t F = state_floats(D);
+    const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (size_t)BH * F) return;
+    const int bh = (int)(gid / F), f = (int)(gid - (size_t)bh * F);
+    const int b = bh / H, h = bh - b * H;
+    const double lam = lambda[(int64_t)b * lam_sb + h];
+    const HeadPtrs hp = in.at(bh, 0, D);
+    const int DD = D * D;
+    float P;
+    if (f < DD) P = hp.S1[f];
+    else if (f < 2 * DD) P = hp.S2[f - DD];
+    else {
+        const int r = f - 2 * DD;
+        P = r < D ? hp.S0[r] : (r < 2 * D ? hp.Z1[r - D] : (r < 3 * D ? hp.Z2[r - 2 * D] : hp.Z0[0]));
+    }
+    const size_t FS = slot_floats(D);
+    float *base = ws + (size_t)bh * nseg * FS + f;
+    for (int sg = 0; sg < nseg; ++sg)
+        base[(size_t)sg * FS] = fmaf((float)pow(lam, (double)sg * seg_len), P, base[(size_t)sg * FS]);
+}
+
 // P <- l^len[b] P + T over user-layout states (pma_state_combine).
 __global__ void state_combine_kernel(int BH, int H, int D, const float *lambda, int64_t lam_sb, double len,
                                      pma_state T, pma_state P) {
@@ -133,6 +160,15 @@ cudaError_t launch_segment_prefix(int BH, int H, int D, int nseg, int seg_len, i
     const int threads = 256;
     const unsigned blocks = (unsigned)((total + threads - 1) / threads);
     segment_prefix_kernel<<<blocks, threads, 0, st>>>(BH, H, D, nseg, seg_len, L, ws, in, final_out, lambda, lam_sb);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_segment_resume(int BH, int H, int D, int nseg, int seg_len, float *ws, const StateRef &in,
+                                  const float *lambda, int64_t lam_sb, cudaStream_t st) {
+    const size_t total = (size_t)BH * state_floats(D);
+    const int threads = 256;
+    const unsigned blocks = (unsigned)((total + threads - 1) / threads);
+    segment_resume_kernel<<<blocks, threads, 0, st>>>(BH, H, D, nseg, seg_len, ws, in, lambda, lam_sb);
     return cudaGetLastError();
 }
 

@@ -60,6 +60,7 @@
 
 #include "prefill.cuh"
 #include "prefill_simt_body.cuh"
+#define PMA_FAULT_AT_EXIT 1  // report expired waits once per CTA, after the final barrier
 #include "tc_common.cuh"
 
 namespace pma {
@@ -97,7 +98,7 @@ struct Small {
     alignas(16) float s0f[3][D];  // S0 entering the chunk, by chunk mod 3
     float z0f[4];                 // Z0 entering the chunk, by chunk mod 3
     uint32_t tmem_base;
-    int abort_flag;
+    CtlShared ctl;
     alignas(16) float cinv_pt[6][C];  // per-token decay: exp(-c_j) of the chunk, one row per mask warp
 };
 constexpr size_t SMEM_BYTES = OFF_SMALL + sizeof(Small) + 1024;
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(512, 1)
     const int U = c_end - c_begin;
     const int n_last = min(C, p.L - (c_end - 1) * C);
     const float kbeta = (PT && p.k_head_scale) ? p.k_head_scale[h] : 1.f;
-    Ctl ctl{&sm.abort_flag, p.status, p.fault};
+    Ctl ctl{&sm.ctl, p.status};
 
     // ---- set-up: powers, barriers, tensor memory
     if (!PT && threadIdx.x <= C) sm.pw[threadIdx.x] = (float)pow((double)lam, (double)threadIdx.x);
@@ -224,7 +225,7 @@ __global__ void __launch_bounds__(512, 1)
             if (i >= B_MLD0 && i <= B_MLD3) n = 32;              // one mask warp
             mbar_init(&sm.bar[i], n);
         }
-        sm.abort_flag = 0;
+        init_ctl(sm.ctl, p.fault);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -247,16 +248,19 @@ __global__ void __launch_bounds__(512, 1)
     __syncthreads();
     const uint32_t tmem = sm.tmem_base;
     uint64_t *bar = sm.bar;
-    bool expired = false;  // test hook: a wait expired before any copy or GEMM was issued
-    if (p.test_wait_ns) {
+    if (p.test_wait_ns) {  // test hook: a wait expires before any copy or GEMM is issued
         if (threadIdx.x == 0) expire_test_wait(&bar[B_NEVER], ctl, p.test_wait_ns, 90);
         __syncthreads();
-        expired = sm.abort_flag != 0;
+        if (ctl.aborted()) {  // the whole CTA: nothing was issued, release tensor memory and leave
+            if (warp == 1)
+                asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(T_COLS)
+                             : "memory");
+            if (threadIdx.x == 0) report_fault(sm.ctl.abort_flag, p.fault);
+            return;
+        }
     }
 
-    if (expired) {
-        // nothing was issued: straight to the release of tensor memory
-    } else if (warp == 0) {
+    if (warp == 0) {
         // ============================== TMA producer
         if (lane == 0) {
             int issued = 0, fetched = 0;
@@ -790,7 +794,7 @@ __global__ void __launch_bounds__(512, 1)
             }
         }
         // ---- final state
-        const bool write_out = ok && !*ctl.abort_flag && p.out.present() &&
+        const bool write_out = ok && !ctl.aborted() && p.out.present() &&
                                (p.state_only || seg == (int)gridDim.y - 1);
         if (write_out) {
             const HeadPtrs dst = p.out.at(bh, p.out.packed ? seg : 0, D);
@@ -823,6 +827,7 @@ __global__ void __launch_bounds__(512, 1)
     tc_fence_after();
     if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(T_COLS) : "memory");
+    if (threadIdx.x == 0) report_fault(sm.ctl.abort_flag, p.fault);
 }
 
 // ------------------------------------------------------------------ host side

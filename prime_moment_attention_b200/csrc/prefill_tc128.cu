@@ -50,6 +50,7 @@
 
 #include "prefill.cuh"
 #include "prefill_simt_body.cuh"
+#define PMA_FAULT_AT_EXIT 1  // report expired waits once per CTA, after the final barrier
 #include "tc_common.cuh"
 
 namespace pma {
@@ -85,7 +86,7 @@ enum { B_FQ, B_FK, B_FV, B_M1, B_M1B, B_M2, B_M3, B_NEVER, NBAR };
 struct Small {
     uint64_t bar[NBAR];
     uint32_t tmem_base;
-    int abort_flag;
+    CtlShared ctl;
     float pw[C + 4];                    // l^t, t = 0..C
     float geo[C + 4];                   // sum_{t<n} l^t
     alignas(16) float cinv[C];          // l^-(1+j)
@@ -183,7 +184,7 @@ __global__ void __launch_bounds__(NT, 1)
     const int c_end = min(c_begin + seg_chunks, nchunks_total);
     const int U = max(c_end - c_begin, 0);
     const int n_last = U > 0 ? min(C, p.L - (c_end - 1) * C) : 0;
-    Ctl ctl{&sm.abort_flag, p.status, p.fault};
+    Ctl ctl{&sm.ctl, p.status};
     uint64_t *bar = sm.bar;
 
     // ---- set-up: powers, barriers, tensor memory, the incoming state
@@ -191,7 +192,7 @@ __global__ void __launch_bounds__(NT, 1)
     if (tid < C) sm.cinv[tid] = (float)pow((double)lam, -1.0 - (double)tid);
     if (tid == 0) {
         for (int i = 0; i < NBAR; ++i) mbar_init(&bar[i], 1);
-        sm.abort_flag = 0;
+        init_ctl(sm.ctl, p.fault);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -199,6 +200,20 @@ __global__ void __launch_bounds__(NT, 1)
                      "r"(T_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (p.test_wait_ns) {  // test hook: a wait expires before any copy or GEMM is issued
+        tc_fence_before();
+        __syncthreads();  // the barriers are initialised, tensor memory allocated
+        tc_fence_after();
+        if (tid == 0) expire_test_wait(&bar[B_NEVER], ctl, p.test_wait_ns, 90);
+        __syncthreads();
+        if (ctl.aborted()) {  // the whole CTA: nothing was issued, release tensor memory and leave
+            if (warp == 0)
+                asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(sm.tmem_base), "r"(T_COLS)
+                             : "memory");
+            if (tid == 0) report_fault(sm.ctl.abort_flag, p.fault);
+            return;
+        }
     }
     float S1r[32], S2r[32];  // S1 / S2 [fl][32 g .. 32 g + 31]
     const bool has_in = !p.state_only && p.in.present();
@@ -225,12 +240,6 @@ __global__ void __launch_bounds__(NT, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    bool expired = false;  // test hook: a wait expired before any copy or GEMM was issued
-    if (p.test_wait_ns) {
-        if (tid == 0) expire_test_wait(&bar[B_NEVER], ctl, p.test_wait_ns, 90);
-        __syncthreads();
-        expired = sm.abort_flag != 0;
-    }
     if (tid == 0) {
         float gs = 0.f;
         for (int j = 0; j <= C; ++j) {
@@ -278,7 +287,7 @@ __global__ void __launch_bounds__(NT, 1)
             }
         }
     };
-    if (tid == 0 && U > 0 && !expired) {
+    if (tid == 0 && U > 0) {
         prefetch_to(PREFETCH);
         const int t0 = c_begin * C;
         if (!SO) load_tile2(OFF_Q, &tq, &bar[B_FQ], t0, h);
@@ -287,7 +296,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     // phases of the four barriers, and which of them have an operation in flight
     uint32_t ph_q = 0, ph_k = 0, ph_v = 0;
-    bool pend_q = !SO && U > 0 && !expired, pend_k = U > 0 && !expired, pend_v = U > 0 && !expired;
+    bool pend_q = !SO && U > 0, pend_k = U > 0, pend_v = U > 0;
     int pend_m = -1;           // latest MMA commit not yet waited for (it covers every earlier MMA)
     uint32_t pend_par = 0;
     fence_proxy_async();  // the state tiles are read by the tensor core
@@ -325,7 +334,7 @@ __global__ void __launch_bounds__(NT, 1)
         }
     };
 
-    bool ok = !expired;
+    bool ok = true;
     for (int u = 0; u < U && ok; ++u) {
         const int n = (u == U - 1) ? n_last : C;
         const int par = u & 1;
@@ -669,7 +678,7 @@ __global__ void __launch_bounds__(NT, 1)
         if (pend_m >= 0) drain(&bar[pend_m], pend_par);
     }
     // ---- final state
-    const bool write_out = ok && !*ctl.abort_flag && p.out.present() &&
+    const bool write_out = ok && !ctl.aborted() && p.out.present() &&
                            (p.state_only || seg == (int)gridDim.y - 1);
     if (write_out) {
         const HeadPtrs dst = p.out.at(bh, p.out.packed ? seg : 0, D);
@@ -687,6 +696,7 @@ __global__ void __launch_bounds__(NT, 1)
     tc_fence_after();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(T_COLS) : "memory");
+    if (tid == 0) report_fault(sm.ctl.abort_flag, p.fault);
 }
 
 template <bool SO, typename TO, bool PRO>

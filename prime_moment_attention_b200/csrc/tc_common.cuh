@@ -56,21 +56,49 @@ __device__ __forceinline__ bool mbar_poll(uint64_t *b, uint32_t parity) {
     return ok != 0;
 }
 
-struct Ctl {
-    volatile int *abort_flag;  // shared: any role gave up
-    int *status;               // global: first failure code (nullable)
-    int *fault;                // the registered fault word (pma_set_fault_word; nullable): device
-                               // memory or pinned host memory, written with a plain store
+// Per-CTA failure record in shared memory.  The fault word's address sits here rather than in Ctl
+// so that the role loops, which pass Ctl around, carry no extra pointer for a path taken only on
+// failure.
+struct CtlShared {
+    int abort_flag;  // 0, or the code of a role that gave up
+    int pad_;
+    int *fault;      // registered fault word (pma_set_fault_word) or nullptr
 };
 
-__device__ __forceinline__ void give_up(const Ctl &ctl, int code) {
-    *ctl.abort_flag = 1;
-    if (ctl.status) atomicCAS(ctl.status, 0, code);
-    if (ctl.fault) {  // a plain store: pinned host memory need not support device atomics
-        volatile int *w = ctl.fault;
+struct Ctl {
+    CtlShared *sh;  // shared
+    int *status;    // global: first failure code (nullable)
+    __device__ __forceinline__ bool aborted() const { return *reinterpret_cast<volatile int *>(&sh->abort_flag) != 0; }
+};
+
+__device__ __forceinline__ void init_ctl(CtlShared &s, int *fault) {
+    s.abort_flag = 0;
+    s.fault = fault;
+}
+
+// The code into the registered fault word (device memory or pinned host memory: a plain store, not
+// an atomic).
+__device__ __forceinline__ void report_fault(int code, int *fault) {
+    if (code && fault) {
+        volatile int *w = fault;
         if (*w == 0) *w = code;
         __threadfence_system();
     }
+}
+
+// Where a kernel reports to the fault word is chosen per translation unit, by what keeps its role
+// loops free of extra register pressure: inside give_up (PMA_FAULT_AT_EXIT 0, the default), or once
+// per CTA after its final barrier (PMA_FAULT_AT_EXIT 1: the kernel calls report_fault itself).
+#ifndef PMA_FAULT_AT_EXIT
+#define PMA_FAULT_AT_EXIT 0
+#endif
+
+__device__ __forceinline__ void give_up(const Ctl &ctl, int code) {
+    *reinterpret_cast<volatile int *>(&ctl.sh->abort_flag) = code;
+    if (ctl.status) atomicCAS(ctl.status, 0, code);
+#if !PMA_FAULT_AT_EXIT
+    report_fault(code, ctl.sh->fault);
+#endif
 }
 
 // Test hook of the failure path: one thread waits for a barrier phase that nothing completes,
@@ -84,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait_slow(uint64_t *b, uint32_t parity, con
     for (uint32_t it = 1;; ++it) {
         if (mbar_try(b, parity)) return true;
         if ((it & 63) == 0) {
-            if (*ctl.abort_flag) return false;
+            if (ctl.aborted()) return false;
             if (gtimer() - t0 > WAIT_NS) {
                 give_up(ctl, code);
                 return false;

@@ -202,7 +202,8 @@ def check_faults(where: str = "prime_moment_attention_b200", synchronize: bool =
 def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
             state: Optional[StateTuple] = None, eps: float = 1.0, return_state: bool = True,
             out_dtype: Optional[torch.dtype] = None, y_out: Optional[torch.Tensor] = None,
-            want_y: bool = True, check: bool = False, prologue: Optional[Prologue] = None):
+            want_y: bool = True, check: bool = False, prologue: Optional[Prologue] = None,
+            workspace: Optional[torch.Tensor] = None, resume: bool = False):
     """Chunked prefill over q, k, v [B,H,L,D] (q pre-scaled by 1/sqrt(D)).
 
     Returns (y [B,H,L,D] or None, final state or None).  `y_out` may be a
@@ -211,7 +212,11 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
     expired) raises KernelFault at the next prefill call of this module, or here with `check=True`,
     which synchronises and reads the call's workspace status word and the fault word.
     With a `prologue`, q, k, v are the raw projections (k, v with H / kv_groups heads)
-    and the kernels apply the GQA map, QK-norm and q scale as they load them."""
+    and the kernels apply the GQA map, QK-norm and q scale as they load them.
+    `workspace` (uint8 device tensor, at least pma_prefill_workspace_bytes) replaces the per-call
+    allocation; with `resume=True` it must be the workspace of a state-only call (want_y=False,
+    state=None) on the same inputs, and the call runs only the output pass from `state`
+    (pma_prefill_resume)."""
     dev = _require_cuda(q, k, v)
     check_faults("prefill")
     if q.dim() != 4:
@@ -250,9 +255,21 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
     else:
         pc, keep = prologue.to_c(D, dev)
         ws_bytes = L_.pma_prefill_ex_workspace_bytes(B, H, L, D, _DT[q.dtype], ctypes.byref(pc))
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    if resume and (prologue is not None or not want_y or workspace is None):
+        raise ValueError("resume=True needs want_y, no prologue and the state-only call's workspace")
+    if workspace is not None:
+        if (workspace.dtype != torch.uint8 or workspace.device != dev or not workspace.is_contiguous()
+                or workspace.numel() < ws_bytes):
+            raise ValueError(f"workspace must be a contiguous uint8 tensor of at least {ws_bytes} bytes on {dev}")
+        ws = workspace if ws_bytes else None
+    else:
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
     wsp = ws.data_ptr() if ws is not None else None
-    if prologue is None:
+    if resume:
+        rc = L_.pma_prefill_resume(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(),
+                                   lam_sb, st_in, st_out, float(eps), ys, wsp, ws_bytes, _stream(dev))
+        _lib.check("pma_prefill_resume", rc)
+    elif prologue is None:
         rc = L_.pma_prefill(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), lam.data_ptr(),
                             lam_sb, st_in, st_out, float(eps), ys, wsp, ws_bytes, _stream(dev))
         _lib.check("pma_prefill", rc)
@@ -267,6 +284,13 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: Decay,
             raise KernelFault(code, "pma_prefill (workspace status word)")
         check_faults("pma_prefill")
     return y, st_out_t
+
+
+def prefill_workspace(q: torch.Tensor) -> torch.Tensor:
+    """A workspace for prefill() calls on inputs shaped like q [B,H,L,D] (no prologue)."""
+    B, H, L, D = q.shape
+    n = _lib.load().pma_prefill_workspace_bytes(B, H, L, D, _DT[q.dtype])
+    return torch.empty(max(n, 1), dtype=torch.uint8, device=q.device)
 
 
 def swiglu(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:

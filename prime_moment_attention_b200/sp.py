@@ -10,13 +10,18 @@ evaluates as its inter-chunk carry (src/prime_moment_attention/chunked_ssd.py:11
   prefix   S_in[g] = l^{L_{g-1}} (... (l^{L_0} S_init + T_0) ...) + T_{g-1}   (pma_state_combine)
   pass 2   y_g, S_out[g] = prefill of shard g from S_in[g]
 
+Inside a GPU a long shard is itself split into segments across SMs; pass 1 leaves the state
+entering each segment (from a zero start) in its workspace, and pass 2 (pma_prefill_resume)
+shifts those by l^start S_in[g] instead of recomputing them, so k and v are read twice, not three
+times.
+
 The exchange is the only collective (an NCCL all-gather of H*(2D^2+3D+1)*4 bytes per
 rank and batch row, over NVLink); there is no data-path traffic.  The final state of the
 whole sequence is S_out[G-1], held by the last rank (broadcast on request).
 
-The per-rank compute goes through `kernels` (a small object with `prefill` and
-`combine`), the CUDA kernels by default; tests substitute a CPU implementation so that
-the collective and prefix logic runs under `gloo` without a GPU.
+The per-rank compute goes through `kernels` (a small object with `shard_state`, `shard_output`
+and `combine`), the CUDA kernels by default; tests substitute a CPU implementation so that the
+collective and prefix logic runs under `gloo` without a GPU.
 """
 from __future__ import annotations
 
@@ -56,9 +61,19 @@ class CudaKernels:
     """The B200 kernels behind `sequence_parallel_prefill` (the default)."""
 
     @staticmethod
-    def prefill(q, k, v, decay, state, eps, want_y, y_out):
+    def shard_state(q, k, v, decay, eps):
+        """Pass 1: the shard's state from zero, and the workspace pass 2 resumes from."""
         from . import ops
-        return ops.prefill(q, k, v, decay, state=state, eps=eps, return_state=True, want_y=want_y, y_out=y_out)
+        ws = ops.prefill_workspace(q)
+        _, T = ops.prefill(q, k, v, decay, eps=eps, return_state=True, want_y=False, workspace=ws)
+        return T, ws
+
+    @staticmethod
+    def shard_output(q, k, v, decay, state, eps, y_out, handle):
+        """Pass 2: y and the final state of the shard from its carried state `state` (None: zero)."""
+        from . import ops
+        return ops.prefill(q, k, v, decay, state=state, eps=eps, return_state=True, y_out=y_out,
+                           workspace=handle, resume=True)
 
     @staticmethod
     def combine(T, P, decay, length):
@@ -86,7 +101,7 @@ def sequence_parallel_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         raise ValueError(f"shard_lengths {lens} do not match world size {G} / this shard's length {Ls}")
 
     # pass 1: this shard's state from zero (k, v only)
-    _, T = kernels.prefill(q, k, v, decay, None, eps, False, None)
+    T, handle = kernels.shard_state(q, k, v, decay, eps)
     mine = flatten_state(T)
     n = mine.numel()
     gathered = torch.empty(G * n, dtype=mine.dtype, device=mine.device)
@@ -102,7 +117,7 @@ def sequence_parallel_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
             kernels.combine(unflatten_state(gathered[g * n:(g + 1) * n], B, H, D), P, decay, lens[g])
 
     # pass 2: the shard from its carried state
-    y, S_out = kernels.prefill(q, k, v, decay, P, eps, True, y_out)
+    y, S_out = kernels.shard_output(q, k, v, decay, P, eps, y_out, handle)
     final = S_out if r == G - 1 else None
     if broadcast_final:
         buf = flatten_state(S_out) if r == G - 1 else torch.empty(n, dtype=mine.dtype, device=mine.device)

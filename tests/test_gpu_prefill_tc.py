@@ -155,3 +155,24 @@ def test_tc128_config5_law_long():
     _, st_only = ops.prefill(q, k, v, lam, want_y=False, check=True)
     for a, b_ in zip(st_only, st32):
         assert_close(a, cpu64(b_), TOL_BF16, "state-only call vs fp32 kernel")
+
+
+@pytest.mark.parametrize("D,dtype", [(64, torch.bfloat16), (128, torch.bfloat16), (64, torch.float32)])
+def test_resume_after_state_only_call(D, dtype):
+    """pma_prefill_resume: a state-only call from zero leaves each segment's entering state in the
+    workspace; the resumed output pass from an incoming state must match the oracle run of the
+    whole sequence from that state (y and final state), as a single pma_prefill call does."""
+    B, H, L = 1, 4, 4096 + 77
+    assert _lib.load().pma_prefill_workspace_bytes(B, H, L, D, ops._DT[dtype]) > 256  # segmented
+    lam = torch.tensor([0.999, 0.99, 0.9999, 0.95])
+    st0 = synth.make_state(B, H, D, lam, seed=18, t0=1000, sigma=0.02, device="cuda")
+    q, k, v = synth.make_qkv(B, H, L, D, seed=19, dtype=dtype, device="cuda")
+    tol = TOL_F32 if dtype == torch.float32 else TOL_BF16
+    ws = ops.prefill_workspace(q)
+    _, T = ops.prefill(q, k, v, lam, want_y=False, workspace=ws, check=True)
+    y, st = ops.prefill(q, k, v, lam, state=st0, out_dtype=torch.float32, workspace=ws, resume=True, check=True)
+    y_ref, st_ref = O.prefill(q, k, v, lam_np(lam), state=tuple(s.cpu() for s in st0))
+    assert_close(y, y_ref, tol, "y")
+    assert_state_close(st, st_ref, tol)
+    _, T_ref = O.prefill(q, k, v, lam_np(lam))
+    assert_state_close(T, T_ref, tol, "zero-start state")

@@ -21,10 +21,19 @@ class OracleKernels:
     """CPU stand-in for the B200 kernels with the same call shapes as sp.CudaKernels."""
 
     @staticmethod
-    def prefill(q, k, v, decay, state, eps, want_y, y_out):
+    def _prefill(q, k, v, decay, state, eps):
         st = None if state is None else tuple(t.double().numpy() for t in state)
         y, s = O.prefill(q.double().numpy(), k.double().numpy(), v.double().numpy(), np.asarray(decay), st, eps)
-        return (torch.from_numpy(y).float() if want_y else None), tuple(torch.from_numpy(a).float() for a in s)
+        return torch.from_numpy(y).float(), tuple(torch.from_numpy(a).float() for a in s)
+
+    @staticmethod
+    def shard_state(q, k, v, decay, eps):
+        return OracleKernels._prefill(q, k, v, decay, None, eps)[1], None
+
+    @staticmethod
+    def shard_output(q, k, v, decay, state, eps, y_out, handle):
+        assert handle is None
+        return OracleKernels._prefill(q, k, v, decay, state, eps)
 
     @staticmethod
     def combine(T, P, decay, length):
