@@ -145,8 +145,10 @@ PMA_API const char *pma_cuda_error_string(int cuda_error);
 PMA_API void pma_set_fault_word(int *word);
 
 /*
- * Test hook for the failure path: with limit_ns > 0, every later tensor-core prefill
- * launch first waits, with that bound, for a barrier phase that nothing completes;
+ * Test hook for the failure path: with limit_ns > 0, every later launch of the moment
+ * prefill on tensor cores (pma_prefill, pma_prefill_ex, pma_prefill_resume,
+ * pma_prefill_no_alloc, pma_selective_prefill; not the delta-rule prefill) first waits,
+ * with that bound, for a barrier phase that nothing completes;
  * the wait expires before any copy or GEMM is issued, the launch records code 90
  * (workspace status word and fault word) and returns without writing outputs.
  * 0 restores normal operation.  For tests only; no counterpart in the reference.

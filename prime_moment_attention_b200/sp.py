@@ -85,14 +85,17 @@ def sequence_parallel_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                               state: Optional[StateTuple] = None, eps: float = 1.0,
                               group: Optional[dist.ProcessGroup] = None, y_out: Optional[torch.Tensor] = None,
                               shard_lengths: Optional[Sequence[int]] = None, broadcast_final: bool = False,
-                              kernels=CudaKernels):
+                              kernels=CudaKernels, validate: bool = False):
     """Prefill of this rank's shard [B, H, Ls, D] of a sequence split over the ranks of `group`.
 
     `state` is the state entering the whole sequence, the same on every rank (None = zero).
     `shard_lengths` gives every rank's Ls (default: all equal to this rank's).  Returns
     (y of this shard, final state of the sequence on the last rank -- or on every rank with
     broadcast_final -- else None).  Every rank takes the same collective steps in the same
-    order, so an exception on one rank surfaces on the others as a collective error or timeout."""
+    order, so an exception on one rank surfaces on the others as a collective error or timeout
+    (the process group's timeout bounds every wait).  validate=True checks every received shard state
+    for non-finite values before folding it (one device synchronisation) and raises ValueError naming
+    the rank it came from; every rank checks the same gathered buffer, so all of them raise."""
     G = dist.get_world_size(group)
     r = dist.get_rank(group)
     B, H, Ls, D = q.shape
@@ -106,6 +109,11 @@ def sequence_parallel_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     n = mine.numel()
     gathered = torch.empty(G * n, dtype=mine.dtype, device=mine.device)
     dist.all_gather_into_tensor(gathered, mine, group=group)
+    if validate:
+        finite = torch.isfinite(gathered.view(G, n)).all(dim=1).tolist()
+        bad = [g for g, ok in enumerate(finite) if not ok]
+        if bad:
+            raise ValueError(f"shard state received from rank(s) {bad} holds non-finite values")
 
     # prefix fold: S_in[r] from the incoming state and shards 0..r-1
     if r == 0:

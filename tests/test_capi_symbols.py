@@ -80,3 +80,20 @@ def test_decode_requires_state():
     rc = L.pma_decode_step(2, 2, 64, ctypes.byref(q), ctypes.byref(q), ctypes.byref(q), 16, 0, None, None, 1.0,
                            ctypes.byref(q), None)
     assert rc == 1
+
+
+def test_torch_operators_register_without_a_gpu():
+    """_pma_torch.so loads on a host without a GPU and registers torch.ops.pma.* with the schemas
+    the Python layer and torch.compile rely on; the fake implementations give output shapes."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    from prime_moment_attention_b200 import torch_ops
+    torch_ops.load()
+    schemas = {str(op._schema).split("(")[0] for op in (torch.ops.pma.prefill.default, torch.ops.pma.decode_step.default,
+                                                         torch.ops.pma.decode_step_.default)}
+    assert schemas == {"pma::prefill", "pma::decode_step", "pma::decode_step_"}
+    with FakeTensorMode():
+        q = torch.empty(2, 3, 10, 64, dtype=torch.bfloat16, device="cuda")
+        y, st = torch.ops.pma.prefill(q, q, q, torch.empty(3, device="cuda"))
+        assert y.shape == q.shape and [tuple(s.shape) for s in st] == [(2, 3, 64), (2, 3, 64, 64), (2, 3, 64, 64),
+                                                                      (2, 3, 1), (2, 3, 64), (2, 3, 64)]
