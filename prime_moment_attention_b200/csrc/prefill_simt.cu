@@ -27,16 +27,26 @@ __global__ void __launch_bounds__(simt_threads<D>()) prefill_simt_kernel(const P
 // place by the state entering each segment:
 //   P_0 = state_in (or 0);  P_{s+1} = l^{len_s} P_s + T_s
 // and optionally write P_nseg (the final state, when T_{nseg-1} is present) to
-// the user's state_out.  One thread per (head-state, float).
+// the user's state_out.  One thread per (head-state, float); one block per head-state
+// and 256 floats (blockIdx.x = head-state), so the decay powers are computed once per
+// block (in double, then rounded) instead of once per float.
 // ---------------------------------------------------------------------------
+constexpr int kCarryThreads = 256;
+
 __global__ void segment_prefix_kernel(int BH, int H, int D, int nseg, int seg_len, int L, float *ws,
                                       StateRef in, StateRef final_out, const float *lambda, int64_t lam_sb) {
+    __shared__ float pw[2];  // l^seg_len, l^(length of the last segment)
     const size_t F = state_floats(D);
-    const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= (size_t)BH * F) return;
-    const int bh = (int)(gid / F), f = (int)(gid - (size_t)bh * F);
+    const int bh = blockIdx.x;
     const int b = bh / H, h = bh - b * H;
-    const double lam = lambda[(int64_t)b * lam_sb + h];
+    if (threadIdx.x < 2) {
+        const double lam = lambda[(int64_t)b * lam_sb + h];
+        pw[threadIdx.x] = (float)pow(lam, (double)(threadIdx.x == 0 ? seg_len : L - (nseg - 1) * seg_len));
+    }
+    __syncthreads();
+    const size_t fi = (size_t)blockIdx.y * blockDim.x + threadIdx.x;
+    if (fi >= F) return;
+    const int f = (int)fi;
     // packed index f -> component pointer offset in a HeadPtrs
     auto comp = [&](const HeadPtrs &hp) -> float * {
         const int DD = D * D;
@@ -56,10 +66,7 @@ __global__ void segment_prefix_kernel(int BH, int H, int D, int nseg, int seg_le
         float T = 0.f;
         if (sg < nprefix) T = base[(size_t)sg * FS];
         base[(size_t)sg * FS] = P;
-        if (sg < nprefix) {
-            const int len = min(seg_len, L - sg * seg_len);
-            P = fmaf((float)pow(lam, (double)len), P, T);
-        }
+        if (sg < nprefix) P = fmaf(pw[sg == nseg - 1 ? 1 : 0], P, T);
     }
     if (final_out.present()) *comp(final_out.at(bh, 0, D)) = P;
 }
@@ -70,12 +77,16 @@ __global__ void segment_prefix_kernel(int BH, int H, int D, int nseg, int seg_le
 // to the state after t tokens.
 __global__ void segment_resume_kernel(int BH, int H, int D, int nseg, int seg_len, float *ws, StateRef in,
                                       const float *lambda, int64_t lam_sb) {
+    __shared__ float pw[kCarryThreads];  // l^(s * seg_len), s < nseg (nseg <= the SM count < 256)
     const size_t F = state_floats(D);
-    const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= (size_t)BH * F) return;
-    const int bh = (int)(gid / F), f = (int)(gid - (size_t)bh * F);
+    const int bh = blockIdx.x;
     const int b = bh / H, h = bh - b * H;
-    const double lam = lambda[(int64_t)b * lam_sb + h];
+    if (threadIdx.x < nseg)
+        pw[threadIdx.x] = (float)pow((double)lambda[(int64_t)b * lam_sb + h], (double)threadIdx.x * seg_len);
+    __syncthreads();
+    const size_t fi = (size_t)blockIdx.y * blockDim.x + threadIdx.x;
+    if (fi >= F) return;
+    const int f = (int)fi;
     const HeadPtrs hp = in.at(bh, 0, D);
     const int DD = D * D;
     float P;
@@ -87,19 +98,22 @@ __global__ void segment_resume_kernel(int BH, int H, int D, int nseg, int seg_le
     }
     const size_t FS = slot_floats(D);
     float *base = ws + (size_t)bh * nseg * FS + f;
-    for (int sg = 0; sg < nseg; ++sg)
-        base[(size_t)sg * FS] = fmaf((float)pow(lam, (double)sg * seg_len), P, base[(size_t)sg * FS]);
+    for (int sg = 0; sg < nseg; ++sg) base[(size_t)sg * FS] = fmaf(pw[sg], P, base[(size_t)sg * FS]);
 }
 
 // P <- l^len[b] P + T over user-layout states (pma_state_combine).
 __global__ void state_combine_kernel(int BH, int H, int D, const float *lambda, int64_t lam_sb, double len,
                                      pma_state T, pma_state P) {
+    __shared__ float pa;  // l^len of this head-state
     const size_t F = state_floats(D);
-    const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= (size_t)BH * F) return;
-    const int bh = (int)(gid / F), f = (int)(gid - (size_t)bh * F);
+    const int bh = blockIdx.x;
     const int b = bh / H, h = bh - b * H;
-    const float a = (float)pow((double)lambda[(int64_t)b * lam_sb + h], len);
+    if (threadIdx.x == 0) pa = (float)pow((double)lambda[(int64_t)b * lam_sb + h], len);
+    __syncthreads();
+    const size_t fi = (size_t)blockIdx.y * blockDim.x + threadIdx.x;
+    if (fi >= F) return;
+    const int f = (int)fi;
+    const float a = pa;
     const int DD = D * D;
     float *pp;
     const float *tp;
@@ -156,28 +170,23 @@ cudaError_t launch_prefill_simt(const PrefillParams &p, int D, int idt, int ydt,
 
 cudaError_t launch_segment_prefix(int BH, int H, int D, int nseg, int seg_len, int L, float *ws, const StateRef &in,
                                   const StateRef &final_out, const float *lambda, int64_t lam_sb, cudaStream_t st) {
-    const size_t total = (size_t)BH * state_floats(D);
-    const int threads = 256;
-    const unsigned blocks = (unsigned)((total + threads - 1) / threads);
-    segment_prefix_kernel<<<blocks, threads, 0, st>>>(BH, H, D, nseg, seg_len, L, ws, in, final_out, lambda, lam_sb);
+    const dim3 grid((unsigned)BH, (unsigned)((state_floats(D) + kCarryThreads - 1) / kCarryThreads));
+    segment_prefix_kernel<<<grid, kCarryThreads, 0, st>>>(BH, H, D, nseg, seg_len, L, ws, in, final_out, lambda, lam_sb);
     return cudaGetLastError();
 }
 
 cudaError_t launch_segment_resume(int BH, int H, int D, int nseg, int seg_len, float *ws, const StateRef &in,
                                   const float *lambda, int64_t lam_sb, cudaStream_t st) {
-    const size_t total = (size_t)BH * state_floats(D);
-    const int threads = 256;
-    const unsigned blocks = (unsigned)((total + threads - 1) / threads);
-    segment_resume_kernel<<<blocks, threads, 0, st>>>(BH, H, D, nseg, seg_len, ws, in, lambda, lam_sb);
+    if (nseg > kCarryThreads) return cudaErrorInvalidValue;
+    const dim3 grid((unsigned)BH, (unsigned)((state_floats(D) + kCarryThreads - 1) / kCarryThreads));
+    segment_resume_kernel<<<grid, kCarryThreads, 0, st>>>(BH, H, D, nseg, seg_len, ws, in, lambda, lam_sb);
     return cudaGetLastError();
 }
 
 cudaError_t launch_state_combine(int B, int H, int D, const float *lambda, int64_t lam_sb, int64_t len,
                                  const pma_state &T, const pma_state &P, cudaStream_t st) {
-    const size_t total = (size_t)B * H * state_floats(D);
-    const int threads = 256;
-    const unsigned blocks = (unsigned)((total + threads - 1) / threads);
-    state_combine_kernel<<<blocks, threads, 0, st>>>(B * H, H, D, lambda, lam_sb, (double)len, T, P);
+    const dim3 grid((unsigned)(B * H), (unsigned)((state_floats(D) + kCarryThreads - 1) / kCarryThreads));
+    state_combine_kernel<<<grid, kCarryThreads, 0, st>>>(B * H, H, D, lambda, lam_sb, (double)len, T, P);
     return cudaGetLastError();
 }
 

@@ -94,7 +94,7 @@ struct Small {
     float pw[C + 4];              // l^t, t = 0..C
     float geo[C + 4];             // sum_{t<n} l^t
     alignas(16) float cinv[C];    // l^-(1+j)
-    alignas(16) float part[NST][4][D];  // per stage and prep warp: column sums of w.v
+    alignas(16) float part[NST][8][D];  // per stage and prep warp: column sums of w.v
     alignas(16) float s0f[3][D];  // S0 entering the chunk, by chunk mod 3
     float z0f[4];                 // Z0 entering the chunk, by chunk mod 3
     uint32_t tmem_base;
@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(512, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Small &sm = *reinterpret_cast<Small *>(smem + OFF_SMALL);
+    constexpr int NPREP = SO ? 8 : 4;  // prep warps (4 + NPREP - 1 is the last)
     const uint32_t sb = su32(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.x, seg = blockIdx.y;
@@ -220,6 +221,7 @@ __global__ void __launch_bounds__(512, 1)
                 i == B_DSFREE1 || i == B_SREADY0 || i == B_SREADY1 || i == B_OEMPTY || i == B_QEMPTY0 ||
                 i == B_QEMPTY1)
                 n = 128;
+            if (SO && i >= B_PREP0 && i <= B_PREP2) n = 32 * NPREP;
             if (i >= B_EMPTY0 && i <= B_EMPTY2) n = 2 + 128;  // two GEMM-group commits + the state warpgroup
             if (i == B_PREADY0 || i == B_PREADY1) n = 128 + 64;  // mask warps 8-11 + helpers 2-3
             if (i >= B_MLD0 && i <= B_MLD3) n = 32;              // one mask warp
@@ -387,13 +389,14 @@ __global__ void __launch_bounds__(512, 1)
             while (!mbar_try(&bar[B_FINAL], 0) && gtimer() - t0 < WAIT_NS) {
             }
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 4 && warp < 4 + NPREP) {
         // ============================== prep: QQ -> tensor memory, KW / K2W tiles, column sums of w.v
+        // (the state-only pass has no mask work, so warps 8-11 join the prep warps there)
         const int tid = threadIdx.x - 128;
         const int wp = warp - 4;
         const int cc = lane & 7;  // K/V tiles: the thread's 16-byte column chunk
-        const int q_base = wp == 0 ? 0 : (wp == 1 ? 12 : (wp == 2 ? 20 : 28));  // first row quad of the warp
-        const int nq_pass = wp == 0 ? 3 : (wp == 3 ? 1 : 2);                    // quads per thread
+        const int q_base = SO ? 4 * wp : (wp == 0 ? 0 : (wp == 1 ? 12 : (wp == 2 ? 20 : 28)));  // first row quad
+        const int nq_pass = SO ? 1 : (wp == 0 ? 3 : (wp == 3 ? 1 : 2));                       // quads per thread
         const uint32_t lane_base = tmem + ((uint32_t)(wp * 32) << 16);
         float4 ld_next = make_float4(0.f, 0.f, 0.f, 0.f);
         if (PT && U > 0) ld_next = load_ld4(ldh, c_begin * C, U == 1 ? n_last : C, lane);
@@ -539,7 +542,7 @@ __global__ void __launch_bounds__(512, 1)
             tc_fence_before();
             mbar_arrive(&bar[B_PREP0 + s]);
         }
-    } else if ((warp >= 8 && warp < 12) || warp == 2 || warp == 3) {
+    } else if (!SO && ((warp >= 8 && warp < 12) || warp == 2 || warp == 3)) {
         // ============================== mask: At -> P
         // TMEM lane quadrant q = warp % 4 holds rows 32q..32q+31, whose P has 2q+2 nonzero 16-column
         // blocks.  Warps 8-11 own the quadrants; warps 2 and 3 take the upper half of the blocks of
@@ -716,7 +719,7 @@ __global__ void __launch_bounds__(512, 1)
             float ds0 = 0.f;
             if (f < D) {
 #pragma unroll
-                for (int w = 0; w < 4; ++w) ds0 += sm.part[s][w][f];
+                for (int w = 0; w < NPREP; ++w) ds0 += sm.part[s][w][f];
             }
             const uint32_t dbase = lane_base + T_A + bb * T_AS + 64;  // [dS | dZ] of chunk u
             const float dz = tmem_ld1(dbase + 64);
