@@ -635,7 +635,7 @@ def bench_sp(args, ws, rank, device, stream, peaks):
     import torch
     from prime_moment_attention_b200 import ops, sp, synth
     hbm_peak, _, peak_kind = peaks
-    c = SP
+    c = dict(SP, L=args.sp_len or SP["L"])
     Ls = c["L"] // ws
     q, k, v = synth.make_qkv(c["B"], c["H"], Ls, c["D"], seed=c["seed"] + 1000 * rank, dtype=torch.bfloat16,
                              device=device)
@@ -666,7 +666,7 @@ def bench_sp(args, ws, rank, device, stream, peaks):
     return {"metric": "sp_prefill_tok_per_s", "value": round(c["B"] * c["L"] / (ms * 1e-3), 1), "unit": "tok/s",
             "ms_per_step": round(ms, 3), "steps": steps, "higher_is_better": True, "scaling": "strong",
             "dtype": "bf16",
-            "config": {"workload": "config5 long-sequence prefill: B=1, H=16, D=128, L=2^20 bf16, per-head lambda "
+            "config": {"workload": f"config5 long-sequence prefill: B=1, H=16, D=128, L={c['L']} bf16, per-head lambda "
                                    f"log-U[0.999,0.99995], {ws} contiguous shard(s) of {Ls} tokens",
                        "path": "pma_prefill (tensor cores at D=128, segments across CTAs)" if ws == 1 else
                                "sequence_parallel_prefill: state-only pass, NCCL all_gather, prefix fold, full pass"},
@@ -879,6 +879,8 @@ def main():
                     help="profiling aid: sequences per GPU for the prefill part (default: config 2's 8)")
     ap.add_argument("--decode-steps", type=int, default=0,
                     help="profiling aid: timed decode steps (default 1000)")
+    ap.add_argument("--sp-len", type=int, default=0,
+                    help="profiling aid: sequence length of the config-5 part (default 2^20)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -72,7 +72,7 @@ def _lam_table(lam, B: int, H: int):
         return np.full((H,), float(lam)), 0
     lam = _f64(lam)
     if lam.ndim == 0 or lam.size == 1:
-        return np.full((H,), float(lam)), 0
+        return np.full((H,), float(lam.reshape(-1)[0])), 0
     if lam.shape == (H,):
         return lam, 0
     if lam.shape == (B, H):

@@ -108,5 +108,7 @@ cudaError_t launch_prefill_tc(const PrefillParams &p, int ydt, dim3 grid, cudaSt
 // q scale exact in bf16).
 bool tc128_supported(int idt);
 cudaError_t launch_prefill_tc128(const PrefillParams &p, int ydt, dim3 grid, cudaStream_t st);
+// State-only pass at D = 128 (y not wanted): one accumulating GEMM per segment (state_tc128.cu).
+cudaError_t launch_state_tc128(const PrefillParams &p, dim3 grid, cudaStream_t st);
 
 }  // namespace pma

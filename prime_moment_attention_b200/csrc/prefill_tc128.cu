@@ -724,7 +724,7 @@ cudaError_t launch_prefill_tc128(const PrefillParams &p, int ydt, dim3 grid, cud
     } else {
         mq = mk;
     }
-    if (so) return tc128::launch_t<true, float, false>(mq, mk, mv, p, grid, st);
+    if (so) return launch_state_tc128(p, grid, st);
     if (p.pro.q_scale != 1.0f)
         return ydt == PMA_F32 ? tc128::launch_t<false, float, true>(mq, mk, mv, p, grid, st)
                               : tc128::launch_t<false, __nv_bfloat16, true>(mq, mk, mv, p, grid, st);

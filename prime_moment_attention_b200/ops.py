@@ -323,11 +323,13 @@ def swiglu(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = N
 
 _copy_streams = {}
 _host_staging = {}  # device index -> (key, (q, k, v, y) device staging buffers)
+_inputs_free = {}   # device index -> event after the last kernels that read the q, k, v staging buffers
 
 
 def release_host_staging():
     """Free the device staging buffers that prefill_from_host keeps between calls."""
     _host_staging.clear()
+    _inputs_free.clear()
 
 
 def _staging(dev, q, k, v, y_dtype):
@@ -337,6 +339,7 @@ def _staging(dev, q, k, v, y_dtype):
     hit = _host_staging.get(dev.index)
     if hit is None or hit[0] != key:
         _host_staging.pop(dev.index, None)
+        _inputs_free.pop(dev.index, None)  # new buffers: the first copies wait for the current stream
         bufs = tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in (q, k, v))
         bufs += (torch.empty(q.shape, dtype=y_dtype, device=dev),)
         hit = (key, bufs)
@@ -383,7 +386,13 @@ def prefill_from_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: 
     h2d, d2h = _copy_stream_pair(dev)
     qd, kd, vd, yd = _staging(dev, q, k, v, y_host.dtype)
     lam, lam_sb = lambda_tensor(decay, B, H, dev)
-    h2d.wait_stream(cur)  # earlier work on the current stream (a previous call's kernels) is done with them
+    free = _inputs_free.get(dev.index)
+    if free is None:
+        h2d.wait_stream(cur)  # fresh staging buffers: everything queued before this call comes first
+    else:
+        # the previous call's kernels are done with the input staging buffers; its last copies back
+        # (device->host, on the other side stream) may still run while these copies in start
+        h2d.wait_event(free)
     states = []
     for i in range(P):
         sl = slice(bounds[i], bounds[i + 1])
@@ -405,6 +414,9 @@ def prefill_from_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay: 
         d2h.wait_event(done)
         with torch.cuda.stream(d2h):
             y_host[sl].copy_(yd[sl], non_blocking=True)
+    free = torch.cuda.Event()
+    free.record(cur)
+    _inputs_free[dev.index] = free
     cur.wait_stream(d2h)  # later work on the current stream (a next call's kernels) follows the copies out
     final = None
     if return_state:

@@ -165,3 +165,25 @@ def test_prefill_from_host_matches_device_prefill(pieces, per_row_decay, with_st
     assert_close(y, cpu64(y_ref), TOL_BF16, "y")
     for a, b in zip(st, st_ref):
         assert_close(a, cpu64(b), TOL_BF16, "state")
+
+
+def test_prefill_from_host_back_to_back_calls():
+    """Three calls in a row with different host inputs of one shape (the staging buffers are reused;
+    a call's input copies may start while the previous call's output copies still run), with no
+    synchronisation between them: every call's y and final state match prefill() on its inputs."""
+    B, H, L, D = 4, 3, 700, 64
+    lam = synth.make_lambdas(H, 0.99, 0.9999, seed=8)
+    cases, outs = [], []
+    for i in range(3):
+        q, k, v = synth.make_qkv(B, H, L, D, seed=50 + i, dtype=torch.bfloat16, device="cuda")
+        cases.append(ops.prefill(q, k, v, lam))
+        qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+        yh = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+        outs.append((qh, kh, vh, yh))
+    torch.cuda.synchronize()
+    results = [ops.prefill_from_host(qh, kh, vh, lam, y_host=yh) for qh, kh, vh, yh in outs]
+    torch.cuda.synchronize()
+    for (y_ref, st_ref), (y, st) in zip(cases, results):
+        assert_close(y, cpu64(y_ref), TOL_BF16, "y")
+        for a, b in zip(st, st_ref):
+            assert_close(a, cpu64(b), TOL_BF16, "state")
