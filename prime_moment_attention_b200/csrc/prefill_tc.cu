@@ -207,8 +207,13 @@ __global__ void __launch_bounds__(512, 1)
     Ctl ctl{&sm.ctl, p.status};
 
     // ---- set-up: powers, barriers, tensor memory
-    if (!PT && threadIdx.x <= C) sm.pw[threadIdx.x] = (float)pow((double)lam, (double)threadIdx.x);
-    if (!PT && threadIdx.x < C) sm.cinv[threadIdx.x] = (float)pow((double)lam, -1.0 - (double)threadIdx.x);
+    if (!PT && threadIdx.x <= C) {  // l^t, sum_{j<t} l^j (closed form, double) and l^-(1+t), t = 0..C
+        const int t = threadIdx.x;
+        const double lt = pow((double)lam, (double)t);
+        sm.pw[t] = (float)lt;
+        sm.geo[t] = (float)(lam == 1.0f ? (double)t : (1.0 - lt) / (1.0 - (double)lam));
+        if (t < C) sm.cinv[t] = (float)(1.0 / (lt * (double)lam));
+    }
     for (int i = threadIdx.x; i < TILE / 16; i += blockDim.x) {  // ones tile: row r = i / 8, chunk i % 8
         const int r = i >> 3, c = i & 7;
         const uint32_t one = (c == (r & 7)) ? 0x3F80u : 0u;  // element 0 of row r sits in chunk 0 ^ (r & 7)
@@ -240,13 +245,6 @@ __global__ void __launch_bounds__(512, 1)
     __syncthreads();
     tc_fence_after();
     fence_proxy_async();  // the ones tile is read by the tensor core
-    if (!PT && threadIdx.x == 0) {
-        float g = 0.f;
-        for (int j = 0; j <= C; ++j) {
-            sm.geo[j] = g;
-            if (j < C) g += sm.pw[j];
-        }
-    }
     __syncthreads();
     const uint32_t tmem = sm.tmem_base;
     uint64_t *bar = sm.bar;
