@@ -514,16 +514,17 @@ def bench_delta(args, ws, rank, device, stream, peaks):
                                   "q/k/v, beta_t=sigmoid(N(0,1)), alpha_t=lambda_h, Lyapunov bound 25"},
            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": peaks[1], "unit": "TFLOP/s",
                         "frac": round(tf / peaks[1], 4), "traffic": None, "peak_kind": peak_kind,
-                        "note": "latency of the sequential chunk recurrence: one CTA per head-state "
-                                f"({min(B * H, 148)} of 148 SMs busy); the float32 triangular solve on the CUDA "
-                                "cores is the longest phase of a chunk",
+                        "note": "WY form: a parallel pass over all (head-state, chunk) units (T^-1 in float32 on "
+                                "CUDA cores, [U | W] = T^-1 [v | exp(cum) Phi] on tensor cores, 72 KB record per "
+                                "unit) then one sequential pass per head-state over the state products "
+                                f"({min(B * H, 148)} of 148 SMs); the parallel pass is the longer one",
                         "fp32_cuda_cores": {"achieved": round(tf, 2), "peak": round(FP32_SIMT_PEAK_TFLOPS, 1),
                                             "frac": round(tf / FP32_SIMT_PEAK_TFLOPS, 4),
                                             "peak_kind": "nominal (148 SMs x 128 FMA/clk x 1965 MHz)"},
                         "hbm": {"achieved": round(bw, 1), "peak": hbm_peak, "unit": "GB/s",
                                 "frac": round(bw / hbm_peak, 4), "peak_kind": peak_kind},
                         "algorithmic_flop_per_launch": tokheads * DELTA_FLOP_PER_TOKHEAD},
-           "gpu_launches": steps, "clocks": clk_r}
+           "gpu_launches": 2 * steps, "clocks": clk_r}
     del q, k, v, y, beta, st
     torch.cuda.empty_cache()
 

@@ -48,7 +48,7 @@
 extern "C" {
 #endif
 
-#define PMA_ABI_VERSION 3
+#define PMA_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define PMA_API __attribute__((visibility("default")))
@@ -359,7 +359,12 @@ PMA_API int pma_decode_step_ex(int N, int H, int D,
  *               lyapunov_bound <= 0 turns it off.
  *   state_in    [B,H,D,2D] or NULL (zero); state_out [B,H,D,2D] or NULL; they may alias.
  *   y           [B,H,L,D] (F32 or BF16) or NULL (state only; then state_out is required).
- * Computed in float32 on CUDA cores (one CTA per head-state, state in shared memory).
+ *   workspace   device scratch of pma_delta_prefill_workspace_bytes(...) bytes, or NULL / 0.
+ * BF16 inputs with D = 64 and chunk 64 run on the tensor cores: with a workspace in the WY form
+ * (every chunk's T^-1 products computed in parallel, then one sequential pass per head-state over
+ * the state-dependent products), without one as a single pass per head-state that solves each
+ * chunk's triangular system in turn.  Other cases are computed in float32 on CUDA cores (one CTA
+ * per head-state, state in shared memory) and need no workspace.
  */
 PMA_API int pma_delta_prefill(int B, int H, int L, int D,
                               const pma_seq_tensor *q, const pma_seq_tensor *k, const pma_seq_tensor *v,
@@ -367,7 +372,18 @@ PMA_API int pma_delta_prefill(int B, int H, int L, int D,
                               const float *lambda, int64_t lambda_stride_b,
                               int chunk, float lyapunov_bound, float norm_eps,
                               const float *state_in, float *state_out,
-                              const pma_seq_tensor *y, pma_stream_t stream);
+                              const pma_seq_tensor *y,
+                              void *workspace, size_t workspace_bytes, pma_stream_t stream);
+
+/*
+ * Bytes of workspace with which pma_delta_prefill takes its WY path (0 when the case has none:
+ * not BF16 / D = 64 / chunk 64, or nothing to compute).  72 KB per (head-state, chunk) of a
+ * window of chunks whose records stay within 1 GiB, plus one state copy per head-state when the
+ * sequence spans several windows.  A smaller workspace runs the sequence in smaller windows; one
+ * that holds less than one chunk per head-state (plus the state copy) is refused with
+ * PMA_ERR_WORKSPACE.  The workspace must be 256-byte aligned.
+ */
+PMA_API size_t pma_delta_prefill_workspace_bytes(int B, int H, int L, int D, int chunk, int dtype);
 
 /*
  * Delta-rule decode step: the L == 1 branch (:142-172), which measures the error against the

@@ -109,8 +109,11 @@ def load() -> ctypes.CDLL:
     L.pma_decode_step_ex.restype = ctypes.c_int
     L.pma_delta_prefill.argtypes = ([ctypes.c_int] * 4 + [_P(SeqTensor)] * 3 + [ctypes.c_void_p] * 3
                                     + [ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_float]
-                                    + [ctypes.c_void_p] * 2 + [_P(SeqTensor), ctypes.c_void_p])
+                                    + [ctypes.c_void_p] * 2 + [_P(SeqTensor), ctypes.c_void_p, ctypes.c_size_t,
+                                                               ctypes.c_void_p])
     L.pma_delta_prefill.restype = ctypes.c_int
+    L.pma_delta_prefill_workspace_bytes.argtypes = [ctypes.c_int] * 6
+    L.pma_delta_prefill_workspace_bytes.restype = ctypes.c_size_t
     L.pma_delta_decode_step.argtypes = ([ctypes.c_int] * 3 + [_P(SeqTensor)] * 3 + [ctypes.c_void_p] * 2
                                         + [ctypes.c_float] * 2 + [ctypes.c_void_p] * 2
                                         + [_P(SeqTensor), ctypes.c_void_p])

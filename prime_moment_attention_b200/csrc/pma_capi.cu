@@ -515,7 +515,8 @@ extern "C" {
 int pma_delta_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,
                       const pma_seq_tensor *v, const float *beta, const float *alpha, const float *lambda,
                       int64_t lambda_stride_b, int chunk, float lyapunov_bound, float norm_eps,
-                      const float *state_in, float *state_out, const pma_seq_tensor *y, pma_stream_t stream) {
+                      const float *state_in, float *state_out, const pma_seq_tensor *y, void *workspace,
+                      size_t workspace_bytes, pma_stream_t stream) {
     if (B < 0 || H <= 0 || L < 0 || !lambda || lambda_stride_b < 0 || !(norm_eps > 0.0f)) return PMA_ERR_ARGUMENT;
     if (D != 16 && D != 32 && D != 64) return PMA_ERR_HEAD_DIM;
     if (chunk != 32 && chunk != 64) return PMA_ERR_ARGUMENT;
@@ -558,10 +559,27 @@ int pma_delta_prefill(int B, int H, int L, int D, const pma_seq_tensor *q, const
     p.state_in = state_in;
     p.state_out = state_out;
     p.fault = g_fault_word.load();
-    cudaError_t e = delta_tc_supported(D, chunk, q->dtype)
-                        ? launch_delta_prefill_tc(p, y ? y->dtype : PMA_F32, st)
-                        : launch_delta_prefill(p, D, chunk, q->dtype, y ? y->dtype : PMA_F32, st);
+    p.test_wait_ns = g_test_wait_ns.load();
+    const int ydt = y ? y->dtype : PMA_F32;
+    cudaError_t e;
+    if (delta_tc_supported(D, chunk, q->dtype)) {
+        if (workspace && workspace_bytes) {
+            const int window = delta_wy_window(B, H, L, workspace_bytes);
+            if (window == 0) return PMA_ERR_WORKSPACE;
+            if ((uintptr_t)workspace % 256) return PMA_ERR_LAYOUT;
+            e = launch_delta_prefill_wy(p, ydt, workspace, window, st);
+        } else {
+            e = launch_delta_prefill_tc(p, ydt, st);
+        }
+    } else {
+        e = launch_delta_prefill(p, D, chunk, q->dtype, ydt, st);
+    }
     return e == cudaSuccess ? PMA_OK : cuda_fail(e);
+}
+
+size_t pma_delta_prefill_workspace_bytes(int B, int H, int L, int D, int chunk, int dtype) {
+    if (!delta_tc_supported(D, chunk, dtype)) return 0;
+    return delta_wy_workspace_bytes(B, H, L);
 }
 
 int pma_delta_decode_step(int N, int H, int D, const pma_seq_tensor *q, const pma_seq_tensor *k,

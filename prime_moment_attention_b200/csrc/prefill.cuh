@@ -64,6 +64,7 @@ struct DeltaParams {
     const float *state_in;    // [B*H][D][2D] or nullptr (zero)
     float *state_out;         // [B*H][D][2D] or nullptr
     int *fault;               // registered fault word or nullptr (tensor-core kernel's expired waits)
+    unsigned long long test_wait_ns;  // test hook (pma_test_expire_waits), WY kernels only
 };
 struct DeltaStepParams {
     int N, H;
@@ -77,6 +78,12 @@ struct DeltaStepParams {
 bool delta_supported(int D, int chunk);
 bool delta_tc_supported(int D, int chunk, int idt);
 cudaError_t launch_delta_prefill_tc(const DeltaParams &p, int ydt, cudaStream_t st);
+// WY form (delta_wy.cu): same cases as the tensor-core kernel, with a workspace; the preferred
+// size is delta_wy_workspace_bytes(B, H, L), and a smaller one runs in windows of
+// delta_wy_window(...) chunks (0: too small).
+size_t delta_wy_workspace_bytes(int B, int H, int L);
+int delta_wy_window(int B, int H, int L, size_t ws_bytes);
+cudaError_t launch_delta_prefill_wy(const DeltaParams &p, int ydt, void *ws, int window, cudaStream_t st);
 cudaError_t launch_delta_prefill(const DeltaParams &p, int D, int chunk, int idt, int ydt, cudaStream_t st);
 cudaError_t launch_delta_step(const DeltaStepParams &p, int D, int idt, int ydt, cudaStream_t st);
 

@@ -553,12 +553,15 @@ def delta_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch
                   alpha: Optional[torch.Tensor], decay: Decay, chunk: int = 64, lyapunov_bound: float = 25.0,
                   norm_eps: float = 1e-5, state: Optional[torch.Tensor] = None, return_state: bool = True,
                   out_dtype: Optional[torch.dtype] = None, y_out: Optional[torch.Tensor] = None,
-                  want_y: bool = True):
+                  want_y: bool = True, wy: bool = True, workspace_bytes: Optional[int] = None):
     """Gated delta-rule chunked prefill (ChunkedGatedDeltaPrimeAttention's L > 1 core).
 
     q (pre-scaled), k, v [B,H,L,D]; beta, alpha [B,H,L] float (alpha None: the decay);
     decay: the module's decay (scalar, [H] or [B,H]) -- the padded tokens of a ragged last
     chunk decay by it, as in the reference; state [B,H,D,2D] float32 or None.
+    wy: give the library the workspace of its WY path (bf16, D = 64, chunk 64); False runs the
+    single-pass tensor-core kernel instead.  workspace_bytes: a smaller workspace than the
+    library's preferred one (the sequence then runs in windows of chunks).
     Returns (y [B,H,L,D] or None, final state [B,H,D,2D] or None)."""
     dev = _require_cuda(q, k, v)
     if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
@@ -587,11 +590,16 @@ def delta_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch
         else:
             y = torch.empty(B, H, L, D, dtype=out_dtype or q.dtype, device=dev)
         ys = ctypes.byref(_seq(y)[0])
+    ws_bytes = L_.pma_delta_prefill_workspace_bytes(B, H, L, D, int(chunk), _DT[q.dtype]) if wy else 0
+    if ws_bytes and workspace_bytes is not None:
+        ws_bytes = int(workspace_bytes)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
     rc = L_.pma_delta_prefill(B, H, L, D, ctypes.byref(qs), ctypes.byref(ks), ctypes.byref(vs), beta.data_ptr(),
                               alpha.data_ptr() if alpha is not None else None, lam.data_ptr(), lam_sb, int(chunk),
                               float(lyapunov_bound), float(norm_eps),
                               st_in.data_ptr() if st_in is not None else None,
-                              st_out.data_ptr() if st_out is not None else None, ys, _stream(dev))
+                              st_out.data_ptr() if st_out is not None else None, ys,
+                              ws.data_ptr() if ws is not None else None, ws_bytes, _stream(dev))
     _lib.check("pma_delta_prefill", rc)
     return y, st_out
 

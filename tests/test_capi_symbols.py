@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_status_strings():
     L = _lib.load()
-    assert L.pma_version() == 3
+    assert L.pma_version() == 4
     for code in range(8):
         assert _lib.status_string(code)
     assert "unknown" in _lib.status_string(99)

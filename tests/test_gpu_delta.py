@@ -134,3 +134,87 @@ def test_delta_argument_errors():
         ops.delta_prefill(q2.cuda(), k2.cuda(), v2.cuda(), b2.cuda(), a2.cuda(), l2.cuda())
     with pytest.raises(ValueError):
         ops.delta_prefill(q.cuda(), k.cuda(), v.cuda(), beta[:, :, :5].cuda(), alpha.cuda(), lam.cuda())
+
+
+WY_CASES = [  # B, H, L, bound, per-token alpha, incoming state
+    (2, 3, 300, 25.0, True, True),
+    (1, 2, 1000, 0.0, False, False),   # projection off
+    (1, 2, 4100, 4.0, True, True),     # projection active over many chunks, ragged tail
+    (3, 1, 64, 25.0, True, False),     # one full chunk
+    (1, 2, 5, 25.0, False, True),      # one short chunk
+]
+
+
+@pytest.mark.parametrize("wy", [True, False], ids=["wy", "single_pass"])
+@pytest.mark.parametrize("B,H,L,bound,pta,with_state", WY_CASES)
+def test_delta_tc_paths_vs_oracle(B, H, L, bound, pta, with_state, wy):
+    """bf16, D = 64, chunk 64: the WY form (prep + sequential kernels, with a workspace) and the
+    single-pass tensor-core kernel (no workspace) against the float64 oracle."""
+    from prime_moment_attention_b200 import ops
+    q, k, v, beta, alpha, lam = _case(B, H, L, 64, seed=L + 7, dtype=torch.bfloat16, per_token_alpha=pta)
+    st = torch.randn(B, H, 64, 128, generator=torch.Generator().manual_seed(8)) * 0.2 if with_state else None
+    y, s = ops.delta_prefill(q.cuda(), k.cuda(), v.cuda(), beta.cuda(), None if alpha is None else alpha.cuda(),
+                             lam.cuda(), lyapunov_bound=bound, state=None if st is None else st.cuda(),
+                             out_dtype=torch.float32, wy=wy)
+    torch.cuda.synchronize()
+    y_ref, s_ref = O.delta_prefill(q, k, v, beta, alpha, lam, chunk=64, bound=bound, state=st)
+    ey = O.rel_err(y.double().cpu().numpy(), y_ref)
+    es = O.rel_err(s.double().cpu().numpy(), s_ref)
+    print(f"delta {'wy' if wy else 'single-pass'} B={B} H={H} L={L}: y {ey:.2e} state {es:.2e}")
+    assert ey <= TOL_BF16 and es <= TOL_BF16
+
+
+def test_delta_wy_windows_match_one_window():
+    """A workspace smaller than the preferred one runs the sequence in windows of chunks, the
+    state carried through state_out (or the workspace when no state is returned).  A window
+    starts from the projected float32 state where one window carries the unprojected bf16 tile
+    and applies the factor after the product, so results agree to bf16 rounding, and both match
+    the oracle."""
+    from prime_moment_attention_b200 import _lib, ops
+    B, H, L = 2, 3, 1000  # 16 chunks
+    q, k, v, beta, alpha, lam = _case(B, H, L, 64, seed=11, dtype=torch.bfloat16, per_token_alpha=True)
+    args = (q.cuda(), k.cuda(), v.cuda(), beta.cuda(), alpha.cuda(), lam.cuda())
+    st = (torch.randn(B, H, 64, 128, generator=torch.Generator().manual_seed(2)) * 0.2).cuda()
+    y1, s1 = ops.delta_prefill(*args, lyapunov_bound=4.0, state=st)
+    per_chunk = B * H * (73728 + 4)
+    small = 3 * per_chunk + 256 + B * H * 64 * 128 * 4  # windows of 3 chunks
+    y2, s2 = ops.delta_prefill(*args, lyapunov_bound=4.0, state=st, workspace_bytes=small)
+    y3, s3 = ops.delta_prefill(*args, lyapunov_bound=4.0, state=st, workspace_bytes=small, return_state=False)
+    torch.cuda.synchronize()
+    assert s3 is None
+    assert torch.equal(y2, y3)  # the carry through the workspace equals the one through state_out
+    assert O.rel_err(y2.double().cpu().numpy(), y1.double().cpu().numpy()) <= 5e-3
+    assert O.rel_err(s2.double().cpu().numpy(), s1.double().cpu().numpy()) <= 5e-3
+    y_ref, s_ref = O.delta_prefill(q, k, v, beta, alpha, lam, chunk=64, bound=4.0, state=st.cpu())
+    assert O.rel_err(y2.double().cpu().numpy(), y_ref) <= TOL_BF16
+    assert O.rel_err(s2.double().cpu().numpy(), s_ref) <= TOL_BF16
+    with pytest.raises(_lib.PmaError):  # not even one chunk per head-state
+        ops.delta_prefill(*args, workspace_bytes=per_chunk // 2)
+
+
+def test_delta_wy_config2_shape():
+    """Config-2 shape (B = 8, H = 12, L = 8192, bf16) with the bench's gates: two sampled
+    head-states against the float64 oracle, all against the single-pass kernel."""
+    from prime_moment_attention_b200 import ops
+    B, H, L = 8, 12, 8192
+    g = torch.Generator().manual_seed(2024)
+    q = (torch.nn.functional.normalize(torch.randn(B, H, L, 64, generator=g), dim=-1) / 8).to(torch.bfloat16)
+    k = torch.randn(B, H, L, 64, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, H, L, 64, generator=g).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(B, H, L, generator=g))
+    lam = torch.exp(torch.empty(H).uniform_(np.log(0.99), np.log(0.9999), generator=g))
+    args = (q.cuda(), k.cuda(), v.cuda(), beta.cuda(), None, lam.cuda())
+    y_wy, s_wy = ops.delta_prefill(*args, lyapunov_bound=25.0, out_dtype=torch.float32)
+    y_sp, s_sp = ops.delta_prefill(*args, lyapunov_bound=25.0, out_dtype=torch.float32, wy=False)
+    torch.cuda.synchronize()
+    e_all = max(O.rel_err(y_wy[b, h].double().cpu().numpy(), y_sp[b, h].double().cpu().numpy())
+                for b in range(B) for h in range(H))
+    for b, h in ((0, 0), (B - 1, H - 1)):
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        y_ref, s_ref = O.delta_prefill(q[sl], k[sl], v[sl], beta[sl], None, lam[h:h + 1], chunk=64, bound=25.0)
+        ey = O.rel_err(y_wy[sl].double().cpu().numpy(), y_ref)
+        es = O.rel_err(s_wy[sl].double().cpu().numpy(), s_ref)
+        print(f"delta wy config 2 head ({b},{h}): y {ey:.2e} state {es:.2e}")
+        assert ey <= TOL_BF16 and es <= TOL_BF16
+    print(f"delta wy vs single-pass, all head-states: {e_all:.2e}")
+    assert e_all <= TOL_BF16

@@ -91,3 +91,22 @@ def test_expired_wait_in_selective_and_module(expiring_waits):
             m(x)
     _lib.load().pma_test_expire_waits(0)
     _normal_call_matches_oracle(q, k, v, lam)
+
+
+def test_expired_wait_in_delta_wy(expiring_waits):
+    """The delta-rule prefill's WY kernels give up too (code 95 from the prep kernel, whose
+    launch comes first) and leave the context usable."""
+    H, L = 2, 300
+    q, k, v = synth.make_qkv(1, H, L, 64, seed=3, dtype=torch.bfloat16, device="cuda")
+    beta = torch.full((1, H, L), 0.5, device="cuda")
+    lam = torch.full((H,), 0.999, device="cuda")
+    ops.delta_prefill(q, k, v, beta, None, lam)
+    torch.cuda.synchronize()
+    assert ops.pending_fault() == 95
+    with pytest.raises(ops.KernelFault):
+        ops.check_faults()
+    _lib.load().pma_test_expire_waits(0)
+    y, s = ops.delta_prefill(q, k, v, beta, None, lam, out_dtype=torch.float32)
+    y_ref, s_ref = O.delta_prefill(q.cpu(), k.cpu(), v.cpu(), beta.cpu(), None, lam.cpu(), chunk=64, bound=25.0)
+    assert O.rel_err(y.double().cpu().numpy(), y_ref) <= TOL_BF16
+    assert O.rel_err(s.double().cpu().numpy(), s_ref) <= TOL_BF16
