@@ -70,7 +70,7 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(NT, 1) delta_tc_kernel(const DeltaParams p) {
     extern __shared__ uint8_t dsm_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *smem = smem_align1024(dsm_raw);
     float *const Tt = reinterpret_cast<float *>(smem + OFF_T);
     float *const VE = reinterpret_cast<float *>(smem + OFF_VE);
     float *const TIv = reinterpret_cast<float *>(smem + OFF_TI);

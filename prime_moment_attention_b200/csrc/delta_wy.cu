@@ -81,7 +81,7 @@ constexpr int P_E0 = 40960;              // exp(cum) Phi rows f 0..63 |  MMA UW 
 constexpr int P_E1 = 49152;              // f 64..127                 /
 constexpr int P_T = 57344;               // T float32 [64][64], xsw layout; then T^-1 hi / lo bf16
 constexpr int P_TH = P_T, P_TL = P_T + 8192;
-constexpr int P_VEC = 73728;             // cum, exp(cum), beta, coef, beta exp(-cum): [5][64] float32
+constexpr int P_VEC = 73728;             // cum, exp(cum), beta, (unused), beta exp(-cum): [5][64] float32
 constexpr int P_BAR = P_VEC + 1280;      // mbarriers, tmem slot, CtlShared
 constexpr int STG_ROW = 144;             // staging row: 128 B + 16 B pad
 constexpr int STG_TILE = C * STG_ROW;
@@ -124,7 +124,7 @@ __device__ __forceinline__ void st4(uint8_t *p, float a, float b, float c, float
 template <typename TI>
 __global__ void __launch_bounds__(PT, 2) delta_wy_prep_kernel(const PrepArgs a) {
     extern __shared__ uint8_t dsm_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *smem = smem_align1024(dsm_raw);
     const DeltaParams &p = a.p;
     uint8_t *const Tb = smem + P_T;
     uint8_t *const Xb = smem + P_X;
@@ -132,8 +132,7 @@ __global__ void __launch_bounds__(PT, 2) delta_wy_prep_kernel(const PrepArgs a) 
     float *const cum = reinterpret_cast<float *>(smem + P_VEC);
     float *const ecum = cum + C;
     float *const bet = ecum + C;
-    float *const coef = bet + C;
-    float *const rbv = coef + C;  // beta_j exp(-cum_j) (ratio form)
+    float *const rbv = bet + 2 * C;  // beta_j exp(-cum_j) (ratio form)
     uint64_t *const bar = reinterpret_cast<uint64_t *>(smem + P_BAR);
     uint64_t *const never = bar + 1;
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(smem + P_BAR + 16);
@@ -231,9 +230,11 @@ __global__ void __launch_bounds__(PT, 2) delta_wy_prep_kernel(const PrepArgs a) 
         uint8_t *rec = a.rec + (size_t)u * REC;
         cp_async_wait_all();
         __syncthreads();
-        // ---- gates (staged with the rows): inclusive scan of log alpha within the chunk (padded
-        // tokens decay by lambda)
-        if (warp == 0) {
+        // ---- gates (staged with the rows): every warp scans log alpha within the chunk itself (two
+        // tokens per lane; padded tokens decay by lambda), so no barrier follows; warp 0 also leaves
+        // the vectors the later phases read
+        float ecm[2], cfm[2];
+        {
             const float *sg = reinterpret_cast<const float *>(smem + P_SG);
             const float glam = sg[2 * C];
             const float lam_c = fminf(fmaxf(glam, 1e-5f), 1.0f);
@@ -257,22 +258,27 @@ __global__ void __launch_bounds__(PT, 2) delta_wy_prep_kernel(const PrepArgs a) 
             la[0] += base;
             la[1] += base;
             const float ce = __shfl_sync(0xffffffffu, la[1], 31);
-            const bool ratio = ce >= RATIO_MIN_CUM;
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
-                const int i = lane * 2 + m;
-                cum[i] = la[m];
-                ecum[i] = __expf(la[m]);
-                bet[i] = gb[m];
-                coef[i] = gb[m] * __expf(ce - la[m]);
-                rbv[i] = ratio ? gb[m] * __expf(-la[m]) : 0.f;
+                ecm[m] = __expf(la[m]);
+                cfm[m] = gb[m] * __expf(ce - la[m]);
             }
-            if (lane == 0) {
-                a.cd[u] = __expf(ce);
-                *ratio_flag = ratio;
+            if (warp == 0) {
+                const bool ratio = ce >= RATIO_MIN_CUM;
+#pragma unroll
+                for (int m = 0; m < 2; ++m) {
+                    const int i = lane * 2 + m;
+                    cum[i] = la[m];
+                    ecum[i] = ecm[m];
+                    bet[i] = gb[m];
+                    rbv[i] = ratio ? gb[m] * __expf(-la[m]) : 0.f;
+                }
+                if (lane == 0) {
+                    a.cd[u] = __expf(ce);
+                    *ratio_flag = ratio;
+                }
             }
         }
-        __syncthreads();
         // ---- features: threads 2r, 2r + 1 hold row r of [Phi ; Psi] (r < 64: k row r, else q row
         // r - 64), 32 input dims each (hf = which half)
         {
@@ -320,9 +326,12 @@ __global__ void __launch_bounds__(PT, 2) delta_wy_prep_kernel(const PrepArgs a) 
                 *reinterpret_cast<uint4 *>(smem + P_A + swz(row, 4 * hf + c)) = pack8(x + 8 * c);
                 *reinterpret_cast<uint4 *>(smem + P_AH + swz(row, 4 * hf + c)) = pack8(y2 + 8 * c);
             }
-            const float e = ecum[i];
+            // exp(cum_i) and coef_i from the lane that scanned token i
+            const float e0 = __shfl_sync(0xffffffffu, ecm[0], i >> 1), e1 = __shfl_sync(0xffffffffu, ecm[1], i >> 1);
+            const float f0 = __shfl_sync(0xffffffffu, cfm[0], i >> 1), f1 = __shfl_sync(0xffffffffu, cfm[1], i >> 1);
+            const float e = (i & 1) ? e1 : e0;
             if (!is_q) {
-                const float cf = coef[i];
+                const float cf = (i & 1) ? f1 : f0;
                 uint8_t *pc = rec + R_PC;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -376,38 +385,45 @@ __global__ void __launch_bounds__(PT, 2) delta_wy_prep_kernel(const PrepArgs a) 
             const int i = (quad & 1) * 32 + lane;
             const bool ratio = *ratio_flag != 0;
             const float ci = cum[i], ei = ecum[i];
-            float g[32], t[32];
-            tmem_ld32(lb + PT_D1 + 32 * hc, g);
 #pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-                float val[4];
-                if (ratio) {  // uniform: exp(cum_i) beta_j exp(-cum_j)
-                    const float4 r4 = *reinterpret_cast<const float4 *>(rbv + 32 * hc + e);
-                    val[0] = ei * r4.x * g[e];
-                    val[1] = ei * r4.y * g[e + 1];
-                    val[2] = ei * r4.z * g[e + 2];
-                    val[3] = ei * r4.w * g[e + 3];
+            for (int hq = 0; hq < 2; ++hq) {  // 16 columns at a time (register pressure)
+                const int j0 = 32 * hc + 16 * hq;
+                uint32_t gr[16];
+                float t[16];
+                tmem_ld16_issue(lb + PT_D1 + j0, gr);
+                tmem_wait_ld_regs(gr);
+#pragma unroll
+                for (int e = 0; e < 16; e += 4) {
+                    float val[4];
+                    if (ratio) {  // uniform: exp(cum_i) beta_j exp(-cum_j)
+                        const float4 r4 = *reinterpret_cast<const float4 *>(rbv + j0 + e);
+                        val[0] = ei * r4.x * __uint_as_float(gr[e]);
+                        val[1] = ei * r4.y * __uint_as_float(gr[e + 1]);
+                        val[2] = ei * r4.z * __uint_as_float(gr[e + 2]);
+                        val[3] = ei * r4.w * __uint_as_float(gr[e + 3]);
+                    } else {
+                        const float4 c4 = *reinterpret_cast<const float4 *>(cum + j0 + e);
+                        const float4 b4 = *reinterpret_cast<const float4 *>(bet + j0 + e);
+                        val[0] = __expf(ci - c4.x) * __uint_as_float(gr[e]) * b4.x;
+                        val[1] = __expf(ci - c4.y) * __uint_as_float(gr[e + 1]) * b4.y;
+                        val[2] = __expf(ci - c4.z) * __uint_as_float(gr[e + 2]) * b4.z;
+                        val[3] = __expf(ci - c4.w) * __uint_as_float(gr[e + 3]) * b4.w;
+                    }
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        const int j = j0 + e + m;
+                        t[e + m] = t_rows ? (j < i ? val[m] : (j == i ? 1.f : 0.f)) : (j <= i ? val[m] : 0.f);
+                    }
+                }
+                if (t_rows) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        st4(Tb + xsw(i, (j0 >> 2) + c), t[4 * c], t[4 * c + 1], t[4 * c + 2], t[4 * c + 3]);
                 } else {
-                    const float4 c4 = *reinterpret_cast<const float4 *>(cum + 32 * hc + e);
-                    const float4 b4 = *reinterpret_cast<const float4 *>(bet + 32 * hc + e);
-                    val[0] = __expf(ci - c4.x) * g[e] * b4.x;
-                    val[1] = __expf(ci - c4.y) * g[e + 1] * b4.y;
-                    val[2] = __expf(ci - c4.z) * g[e + 2] * b4.z;
-                    val[3] = __expf(ci - c4.w) * g[e + 3] * b4.w;
+#pragma unroll
+                    for (int c = 0; c < 2; ++c)
+                        *reinterpret_cast<uint4 *>(rec + R_P + swz(i, (j0 >> 3) + c)) = pack8(t + 8 * c);
                 }
-#pragma unroll
-                for (int m = 0; m < 4; ++m) {
-                    const int j = 32 * hc + e + m;
-                    t[e + m] = t_rows ? (j < i ? val[m] : (j == i ? 1.f : 0.f)) : (j <= i ? val[m] : 0.f);
-                }
-            }
-            if (t_rows) {
-#pragma unroll
-                for (int c = 0; c < 8; ++c) st4(Tb + xsw(i, 8 * hc + c), t[4 * c], t[4 * c + 1], t[4 * c + 2], t[4 * c + 3]);
-            } else {
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    *reinterpret_cast<uint4 *>(rec + R_P + swz(i, 4 * hc + c)) = pack8(t + 8 * c);
             }
         }
         tc_fence_before();
@@ -447,7 +463,8 @@ __global__ void __launch_bounds__(PT, 2) delta_wy_prep_kernel(const PrepArgs a) 
                     const int a_ = blk, b_ = blk + d;
                     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                    for (int kq = 4 * a_; kq < 4 * b_; ++kq) {  // 4 k per step
+                    for (int t = 0; t < 4 * d; ++t) {  // 4 k per step, k = 16 a .. 16 b - 1
+                        const int kq = 4 * a_ + t;
                         const float4 tv = ld4(Tb + xsw(16 * b_ + r, kq));
                         const float tr[4] = {tv.x, tv.y, tv.z, tv.w};
 #pragma unroll
@@ -625,7 +642,7 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16 *dst, const float (&v)
 template <typename TO>
 __global__ void __launch_bounds__(QT, 1) delta_wy_seq_kernel(const SeqArgs a) {
     extern __shared__ uint8_t dsm_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *smem = smem_align1024(dsm_raw);
     const DeltaParams &p = a.p;
     uint64_t *const bar = reinterpret_cast<uint64_t *>(smem + Q_BAR);
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(smem + Q_BAR + NBAR * 8);

@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(NT, 1)
     prefill_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *smem = smem_align1024(smem_raw);
     Small &sm = *reinterpret_cast<Small *>(smem + OFF_SMALL);
     const uint32_t sb = su32(smem);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;

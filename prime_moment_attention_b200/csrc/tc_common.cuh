@@ -16,6 +16,12 @@ constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
 
 // ------------------------------------------------------------------ PTX helpers
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+// The first 1024-byte-aligned byte of a dynamic shared-memory array (128-byte-swizzled tiles need
+// that alignment), as pointer arithmetic on the array itself: the compiler keeps shared-memory
+// accesses through the result in the shared state space.
+__device__ __forceinline__ uint8_t *smem_align1024(uint8_t *raw) {
+    return raw + ((1024u - (su32(raw) & 1023u)) & 1023u);
+}
 
 __device__ __forceinline__ unsigned long long gtimer() {
     unsigned long long t;
