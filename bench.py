@@ -47,7 +47,7 @@ PREFILL_KERNEL_FLOP_PER_TOKHEAD = 2 * 128 * 128 + 2 * 128 * 64 + 2 * 128 * 64 + 
 DECODE_BYTES_PER_HEADSTEP = 2 * (2 * 64 * 64 + 3 * 64 + 1) * 4 + 3 * 64 * 2 + 64 * 2  # 67,592
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of
 # each kernel on the bench workload; the commands and the rest of the numbers are in profiles/.
-PREFILL_TRAFFIC = 305_104_896 + 78_318_848    # prefill_tc_kernel<0, bf16>, config 2
+PREFILL_TRAFFIC = 305_118_208 + 78_783_232    # prefill_tc_kernel<0, bf16>, config 2
 DECODE_TRAFFIC = 1_250_602_000 + 1_183_497_000  # decode_step_kernel<64, bf16, bf16>, config 3
 # Gated delta-rule variant (config 2 with the write gate beta): per token-head of the chunked
 # form at C = 64, F = 2D = 128 features -- Gram Phi Phi^T 2*C*F, intra scores Psi Phi^T 2*C*F,
@@ -55,6 +55,9 @@ DECODE_TRAFFIC = 1_250_602_000 + 1_183_497_000  # decode_step_kernel<64, bf16, b
 # P (beta E) 2*C*D, triangular solve C*D  = 94,208 FLOP; q,k,v in + y out bf16 + beta fp32.
 DELTA_FLOP_PER_TOKHEAD = 4 * 64 * 128 + 6 * 128 * 64 + 3 * 64 * 64
 DELTA_BYTES_PER_TOKHEAD = 8 * 64 + 4
+# DRAM bytes of the WY pair (prep: reads q, k, v, gates, writes the 72 KB records; sequential: reads
+# the records, writes y) from one ncu capture at B = 2 (profiles/), scaled x4 to the B = 8 step
+DELTA_TRAFFIC_B2 = (76_662_784 + 172_416_256) + (226_543_872 + 22_940_160)
 DELTA_DECODE_BYTES_PER_HEADSTEP = 2 * (64 * 128 * 4) + 4 * 64 * 2 + 8  # state rw + q,k,v,y + beta,alpha
 FP32_SIMT_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal: 148 SMs x 128 FMA/clk at 1,965 MHz
 WORKLOAD = ("config2 prefill: B=8 seqs/GPU, H=12, D=64, L=8192, bf16 q/k/v (QK-normed), fp32 state, "
@@ -513,7 +516,8 @@ def bench_delta(args, ws, rank, device, stream, peaks):
                                   "chunk 64, bf16 "
                                   "q/k/v, beta_t=sigmoid(N(0,1)), alpha_t=lambda_h, Lyapunov bound 25"},
            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": peaks[1], "unit": "TFLOP/s",
-                        "frac": round(tf / peaks[1], 4), "traffic": None, "peak_kind": peak_kind,
+                        "frac": round(tf / peaks[1], 4), "traffic": DELTA_TRAFFIC_B2 * B // 2 if B % 2 == 0 else None,
+                        "traffic_note": "both WY kernels, ncu at B=2 scaled to B", "peak_kind": peak_kind,
                         "note": "WY form: a parallel pass over all (head-state, chunk) units (T^-1 in float32 on "
                                 "CUDA cores, [U | W] = T^-1 [v | exp(cum) Phi] on tensor cores, 72 KB record per "
                                 "unit) then one sequential pass per head-state over the state products "
