@@ -48,6 +48,7 @@ DECODE_BYTES_PER_HEADSTEP = 2 * (2 * 64 * 64 + 3 * 64 + 1) * 4 + 3 * 64 * 2 + 64
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of
 # each kernel on the bench workload; the commands and the rest of the numbers are in profiles/.
 PREFILL_TRAFFIC = 305_118_208 + 78_783_232    # prefill_tc_kernel<0, bf16>, config 2
+PREFILL_MIN_WARMUP = 50  # untimed config-2 calls before the timed ones (at least --warmup)
 DECODE_TRAFFIC = 1_250_602_000 + 1_183_497_000  # decode_step_kernel<64, bf16, bf16>, config 3
 # Gated delta-rule variant (config 2 with the write gate beta): per token-head of the chunked
 # form at C = 64, F = 2D = 128 features -- Gram Phi Phi^T 2*C*F, intra scores Psi Phi^T 2*C*F,
@@ -372,7 +373,10 @@ def bench_prefill(args, ws, rank, device, stream, peaks):
 
     clocks = ClockSampler(device.index)
     clocks.start()  # before the warm-up, so that the timed steps follow it back to back
-    ms = time_steps(step, args.steps, args.warmup, ws, device, stream)
+    # at least 50 untimed calls (~8 ms): with several ranks the first calls after the process
+    # group's barrier ran a few per cent slower than the steady state
+    warm = max(args.warmup, PREFILL_MIN_WARMUP)
+    ms = time_steps(step, args.steps, warm, ws, device, stream)
     clk = clocks.stop()
     rank_ms = per_rank(round(ms, 5), ws)
     rank_clk = per_rank(clk, ws)
@@ -404,7 +408,7 @@ def bench_prefill(args, ws, rank, device, stream, peaks):
     def e2e_step():
         ops.prefill_from_host(qh, kh, vh, lam, device=device, y_host=yh, return_state=True)
 
-    e2e_ms = max_over_ranks(time_steps(e2e_step, e2e_steps, 1, ws, device, stream), ws, device)
+    e2e_ms = max_over_ranks(time_steps(e2e_step, e2e_steps, max(3, args.warmup), ws, device, stream), ws, device)
     h2d = 3 * q.numel() * q.element_size()
     d2h = y.numel() * y.element_size()
     return {"metric": "prefill_tok_per_s", "value": round(tokens / (ms * 1e-3), 1), "unit": "tok/s",
@@ -412,7 +416,8 @@ def bench_prefill(args, ws, rank, device, stream, peaks):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "global_batch": B * ws, "seq_len": L,
                        "parallelism": f"dp{ws} (batch x head shards, no collective)",
-                       "l2": "inputs 403 MB per GPU > 126 MB L2; no flush"},
+                       "l2": "inputs 403 MB per GPU > 126 MB L2; no flush",
+                       "warmup_calls": warm},
             "roofline": roof,
             "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
