@@ -49,6 +49,10 @@ DECODE_BYTES_PER_HEADSTEP = 2 * (2 * 64 * 64 + 3 * 64 + 1) * 4 + 3 * 64 * 2 + 64
 # each kernel on the bench workload; the commands and the rest of the numbers are in profiles/.
 PREFILL_TRAFFIC = 305_118_208 + 78_783_232    # prefill_tc_kernel<0, bf16>, config 2
 PREFILL_MIN_WARMUP = 50  # untimed config-2 calls before the timed ones (at least --warmup)
+# DRAM bytes of config 5's one-GPU step (state-only pass over 8 of 9 segments + full pass), from the
+# ncu capture of config 5's heads at L = 2^16 (profiles/prefill_tc128_config5_L65536.md: 478.3 + 4.0
+# MB and 824.7 + 242.8 MB per launch), scaled x16 to L = 2^20 (the plan's segments scale with L)
+SP_TRAFFIC_1GPU = 16 * (478_300_000 + 4_000_000 + 824_700_000 + 242_800_000)
 DECODE_TRAFFIC = 1_250_602_000 + 1_183_497_000  # decode_step_kernel<64, bf16, bf16>, config 3
 # Gated delta-rule variant (config 2 with the write gate beta): per token-head of the chunked
 # form at C = 64, F = 2D = 128 features -- Gram Phi Phi^T 2*C*F, intra scores Psi Phi^T 2*C*F,
@@ -681,7 +685,10 @@ def bench_sp(args, ws, rank, device, stream, peaks):
                        "path": "pma_prefill (tensor cores at D=128, segments across CTAs)" if ws == 1 else
                                "sequence_parallel_prefill: state-only pass, NCCL all_gather, prefix fold, full pass"},
             "roofline": {"bound": "hbm", "achieved": round(bw, 1), "peak": hbm_peak * ws, "unit": "GB/s",
-                         "frac": round(bw / (hbm_peak * ws), 4), "traffic": None,
+                         "frac": round(bw / (hbm_peak * ws), 4),
+                         "traffic": SP_TRAFFIC_1GPU if (ws == 1 and c["L"] == 1 << 20) else None,
+                         "traffic_note": "ncu at L=2^16 scaled x16; 1.44x the algorithmic bytes: the state-only "
+                                         "pass re-reads k, v of 8 of 9 segments",
                          "peak_kind": f"{peak_kind} per GPU x {ws}",
                          "tensor": {"achieved": round(tf, 2), "peak": round(peaks[1] * ws, 1), "unit": "TFLOP/s",
                                     "frac": round(tf / (peaks[1] * ws), 4)},
