@@ -27,6 +27,7 @@ struct PrefillParams {
     const float *logdecay;      // [B*H*L] log lambda_t per token, or nullptr (lambda per head)
     const float *k_head_scale;  // [H] k multiplied by it (the temperature beta_h), or nullptr
     int half_sq;                // 1: user states hold S2, Z2 halved (the selective layout)
+    int y_tma;                  // D = 64 tensor-core kernel: bf16 y rows leave through a TMA store
 };
 
 // Workspace layout: [header: 256 B, int status word first][per-segment states, float32].

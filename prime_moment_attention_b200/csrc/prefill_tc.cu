@@ -72,8 +72,12 @@ constexpr int TILE = C * D * 2;           // [128 x 64] bf16 = 16 KiB
 constexpr int NST = 3;                    // stages of k (-> w.k), v, w.k^2
 constexpr int STAGE = 3 * TILE;
 constexpr int OFF_K = 0, OFF_V = TILE, OFF_K2 = 2 * TILE;
-constexpr int OFF_Q = NST * STAGE;        // two q slots (q is read once, by the prep warps)
-constexpr int OFF_ONES = OFF_Q + 2 * TILE;  // 128 x 64 bf16, column 0 = 1: second N-atom of [V | 1]
+constexpr int OFF_Q = NST * STAGE;        // q slot: the prep warps read it first thing in a chunk and
+                                          // then reload it with the next chunk's q
+constexpr int OFF_YS = OFF_Q + TILE;      // y staging tile (bf16 output): a chunk's rows, one TMA store;
+                                          // the per-token-decay variant uses it as a second q slot that
+                                          // the producer fills with the stage (its prep runs longer)
+constexpr int OFF_ONES = OFF_YS + TILE;   // 128 x 64 bf16, column 0 = 1: second N-atom of [V | 1]
 constexpr int OFF_SB = OFF_ONES + TILE;   // [S1;S2 | Z] bf16, K = 128 features x N = 80, 32-byte swizzle
 constexpr int SB_LBO = 4096;              // next 16-column group
 constexpr int SB_SBO = 256;               // next 8-feature group
@@ -85,7 +89,8 @@ constexpr float LOGMIN = -76.0f;          // per-token decay: smallest chunk sum
 enum {
     B_FULL0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_PREP0, B_PREP1, B_PREP2,
     B_IFULL0, B_IFULL1, B_PREADY0, B_PREADY1, B_DSFULL0, B_DSFULL1, B_DSFREE0, B_DSFREE1,
-    B_QFREE0, B_QFREE1, B_CDONE0, B_CDONE1, B_SREADY0, B_SREADY1, B_OEMPTY, B_QEMPTY0, B_QEMPTY1, B_MLD0, B_MLD1, B_MLD2, B_MLD3,
+    B_QFREE0, B_QFREE1, B_CDONE0, B_CDONE1, B_SREADY0, B_SREADY1, B_OEMPTY, B_QEMPTY0, B_QEMPTY1, B_QFULL, B_MLD0, B_MLD1,
+    B_MLD2, B_MLD3,
     B_FINAL, B_NEVER, NBAR
 };
 
@@ -166,7 +171,8 @@ __device__ __forceinline__ float cum_at(const float c[4], int src, int m) {
 template <bool SO, typename TO, bool PRO, bool PT>
 __global__ void __launch_bounds__(512, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                      const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
+                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap ty,
+                      const PrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_align1024(smem_raw);
     Small &sm = *reinterpret_cast<Small *>(smem + OFF_SMALL);
@@ -272,11 +278,12 @@ __global__ void __launch_bounds__(512, 1)
                     tma_prefetch_l2(&tv, 0, tf, hk, b);
                 }
                 if (!mbar_wait(&bar[B_EMPTY0 + s], ((u / NST) & 1) ^ 1, ctl, 1)) break;
-                if (!SO && !mbar_wait(&bar[B_QEMPTY0 + (u & 1)], ((u >> 1) & 1) ^ 1, ctl, 3)) break;
+                constexpr bool QSTAGE = PT && !SO;  // q of this variant rides with the stage (two slots)
+                if (QSTAGE && !mbar_wait(&bar[B_QEMPTY0 + (u & 1)], ((u >> 1) & 1) ^ 1, ctl, 3)) break;
                 const int t0 = (c_begin + u) * C;
                 uint8_t *base = smem + s * STAGE;
-                mbar_expect_tx(&bar[B_FULL0 + s], SO ? 2 * TILE : 3 * TILE);
-                if (!SO) tma_load(smem + OFF_Q + (u & 1) * TILE, &tq, &bar[B_FULL0 + s], 0, t0, h, b);
+                mbar_expect_tx(&bar[B_FULL0 + s], QSTAGE ? 3 * TILE : 2 * TILE);
+                if (QSTAGE) tma_load(smem + OFF_Q + (u & 1) * TILE, &tq, &bar[B_FULL0 + s], 0, t0, h, b);
                 tma_load(base + OFF_K, &tk, &bar[B_FULL0 + s], 0, t0, hk, b);
                 tma_load(base + OFF_V, &tv, &bar[B_FULL0 + s], 0, t0, hk, b);
                 issued = u + 1;
@@ -398,6 +405,15 @@ __global__ void __launch_bounds__(512, 1)
         const uint32_t lane_base = tmem + ((uint32_t)(wp * 32) << 16);
         float4 ld_next = make_float4(0.f, 0.f, 0.f, 0.f);
         if (PT && U > 0) ld_next = load_ld4(ldh, c_begin * C, U == 1 ? n_last : C, lane);
+        // the q slot: thread 0 of the prep warps loads chunk 0's q now and each next chunk's q once
+        // every prep thread has read the current one (L2-prefetched by the producer)
+        const bool q_loader = !SO && !PT && tid == 0;
+        int q_issued = 0;
+        if (q_loader && U > 0) {
+            mbar_expect_tx(&bar[B_QFULL], TILE);
+            tma_load(smem + OFF_Q, &tq, &bar[B_QFULL], 0, c_begin * C, h, b);
+            q_issued = 1;
+        }
         for (int u = 0, s = 0; u < U; ++u, s = (s == NST - 1) ? 0 : s + 1) {
             const int bb = u & 1;
             const int n = (u == U - 1) ? n_last : C;
@@ -410,11 +426,23 @@ __global__ void __launch_bounds__(512, 1)
             if (!mbar_wait(&bar[B_FULL0 + s], (u / NST) & 1, ctl, 7)) break;
             uint8_t *k_s = smem + s * STAGE + OFF_K, *v_s = smem + s * STAGE + OFF_V, *k2_s = smem + s * STAGE + OFF_K2;
             uint4 xq[8];  // row tid of q, kept in registers until its tensor-memory buffer is free
-            if (!SO) {
+            if (!SO && PT) {  // two slots, filled by the producer with the stage
                 const uint8_t *q_s = smem + OFF_Q + bb * TILE;
 #pragma unroll
                 for (int c = 0; c < 8; ++c) xq[c] = *reinterpret_cast<const uint4 *>(q_s + swz(tid, c));
                 mbar_arrive(&bar[B_QEMPTY0 + bb]);  // the q slot may be reloaded
+            } else if (!SO) {
+                if (!mbar_wait(&bar[B_QFULL], u & 1, ctl, 4)) break;
+                const uint8_t *q_s = smem + OFF_Q;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) xq[c] = *reinterpret_cast<const uint4 *>(q_s + swz(tid, c));
+                mbar_arrive(&bar[B_QEMPTY0]);  // the q slot may be reloaded
+                if (q_loader && u + 1 < U) {
+                    if (!mbar_wait(&bar[B_QEMPTY0], u & 1, ctl, 3)) break;
+                    mbar_expect_tx(&bar[B_QFULL], TILE);
+                    tma_load(smem + OFF_Q, &tq, &bar[B_QFULL], 0, (c_begin + u + 1) * C, h, b);
+                    q_issued = u + 2;
+                }
             }
             // KW = w.k in place and K2W = KW.k (packed bf16 products), and the column sums of w.v
             // (float32).  Items of 4 rows x one 16-byte column chunk; the row quads are split
@@ -540,6 +568,12 @@ __global__ void __launch_bounds__(512, 1)
             tc_fence_before();
             mbar_arrive(&bar[B_PREP0 + s]);
         }
+        // no copy may still target this CTA's shared memory at exit: the last q load issued
+        if (q_loader && q_issued > 0) {
+            const unsigned long long w0 = gtimer();
+            while (!mbar_try(&bar[B_QFULL], (q_issued - 1) & 1) && gtimer() - w0 < WAIT_NS) {
+            }
+        }
     } else if (!SO && ((warp >= 8 && warp < 12) || warp == 2 || warp == 3)) {
         // ============================== mask: At -> P
         // TMEM lane quadrant q = warp % 4 holds rows 32q..32q+31, whose P has 2q+2 nonzero 16-column
@@ -642,6 +676,9 @@ __global__ void __launch_bounds__(512, 1)
         // ============================== state: S += dS, bf16 state tile for the carry GEMM
         const int wq = warp - 12;
         const int f = wq * 32 + lane;  // feature row: f < 64 -> S1 row f, else S2 row f - 64
+        // bf16 rows leave through the staging tile and a TMA store per chunk (warp-uniform).  The
+        // per-token-decay variant keeps its own row stores: the staging path costs it registers.
+        const bool use_tma_y = !SO && !PT && sizeof(TO) == 2 && p.y_tma != 0;
         const uint32_t lane_base = tmem + ((uint32_t)(wq * 32) << 16);
         float S[D];
         float Z, s0 = 0.f, Z0;
@@ -756,6 +793,10 @@ __global__ void __launch_bounds__(512, 1)
                 break;
             }
             tc_fence_after();
+            if (use_tma_y) {  // the previous chunk's store has read the staging tile
+                if (f == 0) bulk_wait_read();
+                named_bar(1, 128);
+            }
             {
                 uint32_t r[32], r64;
                 tmem_ld33(lane_base + T_ACC, r, r64);  // columns 0..31 and the denominator column
@@ -784,7 +825,14 @@ __global__ void __launch_bounds__(512, 1)
                         r[4 * e4 + 2] = __float_as_uint(hi.x);
                         r[4 * e4 + 3] = __float_as_uint(hi.y);
                     }
-                    if (f < n) store_row32<TO>(yrow + 32 * hc, reinterpret_cast<const float *>(r));
+                    if (use_tma_y) {  // row f of the staging tile, columns 32 hc ..
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            *reinterpret_cast<uint4 *>(smem + OFF_YS + swz(f, 4 * hc + c)) =
+                                pack8(reinterpret_cast<const float *>(r) + 8 * c);
+                    } else if (f < n) {
+                        store_row32<TO>(yrow + 32 * hc, reinterpret_cast<const float *>(r));
+                    }
                 };
                 half(0);
                 tmem_ld32_issue(lane_base + T_ACC + 32, r);
@@ -793,7 +841,16 @@ __global__ void __launch_bounds__(512, 1)
                 mbar_arrive(&bar[B_OEMPTY]);  // ACC is in registers: the next chunk's carry GEMM may start
                 half(1);
             }
+            if (use_tma_y) {  // the chunk's rows as one TMA store (rows past L are not written)
+                fence_proxy_async();
+                named_bar(2, 128);
+                if (f == 0) {
+                    tma_store(&ty, smem + OFF_YS, 0, (c_begin + u) * C, h, b);
+                    bulk_commit();
+                }
+            }
         }
+        if (use_tma_y && f == 0) bulk_wait_all();  // every row store is complete before the CTA ends
         // ---- final state
         const bool write_out = ok && !ctl.aborted() && p.out.present() &&
                                (p.state_only || seg == (int)gridDim.y - 1);
@@ -871,11 +928,19 @@ bool make_tile_map(CUtensorMap *m, const Seq &s, int B, int H, int L, int Dh) {
 
 template <bool SO, typename TO, bool PRO, bool PT>
 static cudaError_t launch_t(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
-                            const PrefillParams &p, dim3 grid, cudaStream_t st) {
+                            const PrefillParams &p0, dim3 grid, cudaStream_t st) {
     auto kern = prefill_tc_kernel<SO, TO, PRO, PT>;
     cudaError_t e = set_smem_once<prefill_tc_kernel<SO, TO, PRO, PT>>((int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    kern<<<grid, 512, SMEM_BYTES, st>>>(mq, mk, mv, p);
+    // bf16 y rows: a tensor map for the chunk stores (else the kernel stores rows itself)
+    PrefillParams p = p0;
+    CUtensorMap my = mq;
+    p.y_tma = 0;
+    if (!SO && !PT && sizeof(TO) == 2 && p.y.p) {
+        const Seq ys{p.y.p, p.y.sb, p.y.sh, p.y.sl};
+        if (make_tile_map(&my, ys, p.B, p.H, p.L, 64)) p.y_tma = 1;
+    }
+    kern<<<grid, 512, SMEM_BYTES, st>>>(mq, mk, mv, my, p);
     return cudaGetLastError();
 }
 
