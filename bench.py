@@ -47,7 +47,7 @@ PREFILL_KERNEL_FLOP_PER_TOKHEAD = 2 * 128 * 128 + 2 * 128 * 64 + 2 * 128 * 64 + 
 DECODE_BYTES_PER_HEADSTEP = 2 * (2 * 64 * 64 + 3 * 64 + 1) * 4 + 3 * 64 * 2 + 64 * 2  # 67,592
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of
 # each kernel on the bench workload; the commands and the rest of the numbers are in profiles/.
-PREFILL_TRAFFIC = 305_118_208 + 78_783_232    # prefill_tc_kernel<0, bf16>, config 2
+PREFILL_TRAFFIC = 306_312_192 + 79_452_160    # prefill_tc_kernel<0, bf16>, config 2
 PREFILL_MIN_WARMUP = 50  # untimed config-2 calls before the timed ones (at least --warmup)
 # DRAM bytes of config 5's one-GPU step (state-only pass over 8 of 9 segments + full pass), from the
 # ncu capture of config 5's heads at L = 2^16 (profiles/prefill_tc128_config5_L65536.md: 478.3 + 4.0
