@@ -176,3 +176,23 @@ def test_resume_after_state_only_call(D, dtype):
     assert_state_close(st, st_ref, tol)
     _, T_ref = O.prefill(q, k, v, lam_np(lam))
     assert_state_close(T, T_ref, tol, "zero-start state")
+
+
+@pytest.mark.parametrize("L", [300, 4173])
+def test_tc_y_rows_into_a_strided_view(L):
+    """bf16 y leaves the D = 64 kernel through a staging tile and one TMA store per chunk: into
+    a view of a wider buffer (row stride 128 elements), with a ragged last chunk (and, at L =
+    4173, the sequence split into segments across CTAs), the rows equal those written into a
+    contiguous y, and nothing around the view is touched."""
+    B, H, D = 2, 3, 64
+    q, k, v = synth.make_qkv(B, H, L, D, seed=L + 1, dtype=torch.bfloat16, device="cuda")
+    lam = synth.make_lambdas(H, 0.99, 0.9999, seed=2)
+    y_ref, _ = ops.prefill(q, k, v, lam, out_dtype=torch.bfloat16, check=True)
+    wide = torch.full((B, H, L + 3, 2 * D), 7.0, dtype=torch.bfloat16, device="cuda")
+    view = wide[:, :, :L, :D]
+    ops.prefill(q, k, v, lam, y_out=view, check=True)
+    torch.cuda.synchronize()
+    assert torch.equal(view, y_ref)
+    assert bool((wide[:, :, :, D:] == 7.0).all()) and bool((wide[:, :, L:, :] == 7.0).all())
+    y64, _ = O.prefill(q, k, v, lam_np(lam))
+    assert_close(view, y64, TOL_BF16, "y (strided view)")
