@@ -83,10 +83,13 @@ class ClockSampler:
     """nvidia-smi clock/throttle samples taken during the timed region."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+         "clocks_event_reasons.sw_power_cap,clocks.mem")
 
     def __init__(self, index: int):
-        self.index = index
+        # nvidia-smi numbers the physical GPUs: map the CUDA device index through CUDA_VISIBLE_DEVICES
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        self.index = ids[index] if index < len(ids) else index
         self.proc = None
         self.path = None
 
@@ -118,10 +121,13 @@ class ClockSampler:
         if not rows:
             return None
         sm = sorted(int(r[1]) for r in rows)
+        mem = sorted(int(r[9]) for r in rows if len(r) > 9 and r[9].isdigit())
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": int(rows[0][2]), "samples": len(rows),
-                "reasons": reasons}
+        out = {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": int(rows[0][2]), "samples": len(rows), "reasons": reasons}
+        if mem:
+            out["mem_mhz"] = mem[len(mem) // 2]
+        return out
 
 
 # --------------------------------------------------------------------------- distributed
