@@ -81,8 +81,8 @@ constexpr int P_E0 = 40960;              // exp(cum) Phi rows f 0..63 |  MMA UW 
 constexpr int P_E1 = 49152;              // f 64..127                 /
 constexpr int P_T = 57344;               // T float32 [64][64], xsw layout; then T^-1 hi / lo bf16
 constexpr int P_TH = P_T, P_TL = P_T + 8192;
-constexpr int P_VEC = 73728;             // cum, exp(cum), beta, (unused), beta exp(-cum): [5][64] float32
-constexpr int P_BAR = P_VEC + 1280;      // mbarriers, tmem slot, CtlShared
+constexpr int P_VEC = 73728;             // cum, exp(cum), beta, beta exp(-cum): [4][64] float32
+constexpr int P_BAR = P_VEC + 1024;      // mbarriers, tmem slot, CtlShared
 constexpr int STG_ROW = 144;             // staging row: 128 B + 16 B pad
 constexpr int STG_TILE = C * STG_ROW;
 constexpr int P_STG = P_BAR + 64;        // next unit's k, q, v rows
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(PT, 2) delta_wy_prep_kernel(const PrepArgs a) 
     float *const cum = reinterpret_cast<float *>(smem + P_VEC);
     float *const ecum = cum + C;
     float *const bet = ecum + C;
-    float *const rbv = bet + 2 * C;  // beta_j exp(-cum_j) (ratio form)
+    float *const rbv = bet + C;  // beta_j exp(-cum_j) (ratio form)
     uint64_t *const bar = reinterpret_cast<uint64_t *>(smem + P_BAR);
     uint64_t *const never = bar + 1;
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(smem + P_BAR + 16);
@@ -566,9 +566,9 @@ __global__ void __launch_bounds__(PT, 2) delta_wy_prep_kernel(const PrepArgs a) 
                 }
             }
         }
+        // no barrier here: the next unit's first barrier (after its staged rows land) orders these
+        // tensor-memory reads before its GEMMs, and the gate scan before it touches nothing read here
         tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
     }
 
     cp_async_wait_all();  // no copy may still target this CTA's shared memory at exit
