@@ -430,13 +430,13 @@ __global__ void __launch_bounds__(512, 1)
                 const uint8_t *q_s = smem + OFF_Q + bb * TILE;
 #pragma unroll
                 for (int c = 0; c < 8; ++c) xq[c] = *reinterpret_cast<const uint4 *>(q_s + swz(tid, c));
-                mbar_arrive(&bar[B_QEMPTY0 + bb]);  // the q slot may be reloaded
+                mbar_arrive_after_reads(&bar[B_QEMPTY0 + bb]);  // the q slot may be reloaded
             } else if (!SO) {
                 if (!mbar_wait(&bar[B_QFULL], u & 1, ctl, 4)) break;
                 const uint8_t *q_s = smem + OFF_Q;
 #pragma unroll
                 for (int c = 0; c < 8; ++c) xq[c] = *reinterpret_cast<const uint4 *>(q_s + swz(tid, c));
-                mbar_arrive(&bar[B_QEMPTY0]);  // the q slot may be reloaded
+                mbar_arrive_after_reads(&bar[B_QEMPTY0]);  // the q slot may be reloaded
                 if (q_loader && u + 1 < U) {
                     if (!mbar_wait(&bar[B_QEMPTY0], u & 1, ctl, 3)) break;
                     mbar_expect_tx(&bar[B_QFULL], TILE);
@@ -765,7 +765,7 @@ __global__ void __launch_bounds__(512, 1)
                 if (h2 == 1) {
                     tc_fence_before();
                     mbar_arrive(&bar[B_DSFREE0 + bb]);
-                    mbar_arrive(&bar[B_EMPTY0 + s]);
+                    mbar_arrive_after_reads(&bar[B_EMPTY0 + s]);  // part[s] is rewritten after the refill
                 }
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {

@@ -144,6 +144,14 @@ __device__ __forceinline__ void expire_test_wait(uint64_t *never, const Ctl &ctl
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Hands back a shared-memory buffer that this thread has read with ordinary loads, to a copy that
+// rewrites it (a TMA or bulk copy issued once the barrier phase completes, or work ordered after
+// such a copy).  The arrive alone does not order the generic-proxy reads before the async-proxy
+// writes: without the proxy fence the copy can land before the loads are performed.
+__device__ __forceinline__ void mbar_arrive_after_reads(uint64_t *b) {
+    fence_proxy_async();
+    mbar_arrive(b);
+}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }

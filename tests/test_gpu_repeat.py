@@ -1,0 +1,73 @@
+"""Repeated D = 64 tensor-core prefills (constant and per-token decay) give bit-identical outputs
+while other kernels churn device memory and shared memory between the calls.
+
+The case is the one where a q-slot release raced the refill of that slot: an incoming state (the
+state warps publish the first carry tile late), three chunks (the third chunk's q reuses the first
+chunk's slot) and one CTA per head-state on most SMs.  The prep warps' generic reads of the slot
+must be ordered before the TMA refill by a proxy fence; without it the first chunk's rows came out
+with the third chunk's q in some of their columns in about one call out of three."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import TOL_BF16
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+B, H, L, D = 4, 16, 300, 64
+REPEATS = 40
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(11)
+    q = torch.nn.functional.normalize(torch.randn(B, H, L, D, generator=g), dim=-1) / D ** 0.5
+    k = torch.nn.functional.normalize(torch.randn(B, H, L, D, generator=g), dim=-1)
+    v = torch.randn(B, H, L, D, generator=g)
+    tau = torch.exp(torch.empty(H).uniform_(1.1, 7.6, generator=g))
+    ld = -(torch.nn.functional.softplus(torch.randn(B, H, L, generator=g)) / tau.view(1, H, 1))
+    beta = torch.exp(0.3 * torch.randn(H, generator=g))
+    st = [torch.randn(B, H, *sh, generator=g) * 0.05 for sh in [(D,), (D, D), (D, D), (1,), (D,), (D,)]]
+    st[3] = st[3].abs() + 20.0
+    return q.bfloat16(), k.bfloat16(), v.bfloat16(), ld, beta, tuple(st)
+
+
+def _churn(i):
+    """Device-memory traffic between calls: large fills, then a big prefill that leaves its own
+    tiles in every SM's shared memory."""
+    from prime_moment_attention_b200 import ops
+    bufs = [torch.empty(1 << s, dtype=torch.float32, device="cuda").fill_(float(i) * 1e3) for s in (16, 20, 22, 24)]
+    del bufs
+    if i % 3 == 2:
+        x = torch.full((4, 16, 2048, D), 0.01 * (i % 7), dtype=torch.bfloat16, device="cuda")
+        ops.prefill(x, x, x, 0.99, return_state=False)
+
+
+@pytest.mark.parametrize("variant", ["per_token_decay", "constant_decay"])
+def test_repeat_calls_bit_identical(variant):
+    from prime_moment_attention_b200 import ops
+    q, k, v, ld, beta, st = _inputs()
+    qc, kc, vc, ldc, bc = q.cuda(), k.cuda(), v.cuda(), ld.cuda(), beta.cuda()
+    stc = tuple(t.cuda() for t in st)
+    if variant == "per_token_decay":
+        call = lambda: ops.selective_prefill(qc, kc, vc, ldc, bc, state=stc, out_dtype=torch.float32)
+    else:
+        pst = ops.new_state(B, H, D, "cuda")
+        for a, b in zip(pst, st):  # same parts, same order, one allocation
+            a.copy_(b.reshape(a.shape))
+        call = lambda: ops.prefill(qc, kc, vc, 0.995, state=pst, out_dtype=torch.float32)
+    y0, s0 = call()
+    torch.cuda.synchronize()
+    y0, s0 = y0.clone(), [t.clone() for t in s0]
+    if variant == "per_token_decay":  # the first result is the right one
+        y_ref, _ = O.selective_prefill(q, k, v, ld, beta, st)
+        assert O.rel_err(y0.double().cpu().numpy(), y_ref) <= TOL_BF16
+    bad = []
+    for i in range(REPEATS):
+        _churn(i)
+        y, s = call()
+        torch.cuda.synchronize()
+        if not torch.equal(y, y0) or not all(torch.equal(a, b) for a, b in zip(s, s0)):
+            rows = ((y - y0).abs().amax(dim=-1) > 0).nonzero()
+            bad.append((i, int(rows[:, 2].min()) if len(rows) else None, int(rows[:, 2].max()) if len(rows) else None))
+    assert not bad, f"calls whose output differs from the first (call, first row, last row): {bad[:5]}"
