@@ -117,17 +117,45 @@ constexpr uint32_t T_A = 0, T_AS = 144, T_QQ = 288, T_ACC = 416, T_COLS = 512;
 
 template <typename TO>
 __device__ __forceinline__ void store_row32(TO *dst, const float *v);
+// 32 bytes in one store (the row's address 32-byte aligned)
+__device__ __forceinline__ void st_global_v8(void *dst, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t a4,
+                                             uint32_t a5, uint32_t a6, uint32_t a7) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(a0), "r"(a1), "r"(a2),
+                 "r"(a3), "r"(a4), "r"(a5), "r"(a6), "r"(a7)
+                 : "memory");
+}
+// A thread's row stores: 32-byte stores where the row allows, which halves the store instructions
+// and the L1 requests of the scattered per-thread rows.
 template <>
 __device__ __forceinline__ void store_row32<__nv_bfloat16>(__nv_bfloat16 *dst, const float *v) {
-    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) d[c] = pack8(v + 8 * c);
+        for (int c = 0; c < 2; ++c) {
+            const float *w = v + 16 * c;
+            st_global_v8(dst + 16 * c, pack2(w[0], w[1]), pack2(w[2], w[3]), pack2(w[4], w[5]), pack2(w[6], w[7]),
+                         pack2(w[8], w[9]), pack2(w[10], w[11]), pack2(w[12], w[13]), pack2(w[14], w[15]));
+        }
+    } else {
+        uint4 *d = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) d[c] = pack8(v + 8 * c);
+    }
 }
 template <>
 __device__ __forceinline__ void store_row32<float>(float *dst, const float *v) {
-    float4 *d = reinterpret_cast<float4 *>(dst);
+    if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
 #pragma unroll
-    for (int c = 0; c < 8; ++c) d[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        for (int c = 0; c < 4; ++c) {
+            const float *w = v + 8 * c;
+            st_global_v8(dst + 8 * c, __float_as_uint(w[0]), __float_as_uint(w[1]), __float_as_uint(w[2]),
+                         __float_as_uint(w[3]), __float_as_uint(w[4]), __float_as_uint(w[5]), __float_as_uint(w[6]),
+                         __float_as_uint(w[7]));
+        }
+    } else {
+        float4 *d = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) d[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    }
 }
 
 // ------------------------------------------------------------------ per-token decay helpers

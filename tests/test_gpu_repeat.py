@@ -1,5 +1,6 @@
-"""Repeated D = 64 tensor-core prefills (constant and per-token decay) give bit-identical outputs
-while other kernels churn device memory and shared memory between the calls.
+"""D = 64 tensor-core prefills (constant and per-token decay): repeated calls give bit-identical
+outputs while other kernels churn device memory and shared memory between the calls, and the
+per-thread output rows land the same through views of any 16-byte alignment.
 
 The case is the one where a q-slot release raced the refill of that slot: an incoming state (the
 state warps publish the first carry tile late), three chunks (the third chunk's q reuses the first
@@ -71,3 +72,31 @@ def test_repeat_calls_bit_identical(variant):
             rows = ((y - y0).abs().amax(dim=-1) > 0).nonzero()
             bad.append((i, int(rows[:, 2].min()) if len(rows) else None, int(rows[:, 2].max()) if len(rows) else None))
     assert not bad, f"calls whose output differs from the first (call, first row, last row): {bad[:5]}"
+
+
+@pytest.mark.parametrize("variant,out_dtype", [("per_token_decay", torch.bfloat16), ("per_token_decay", torch.float32),
+                                               ("constant_decay", torch.float32)])
+def test_row_stores_into_views_of_mixed_alignment(variant, out_dtype):
+    """Output rows that threads store one row each (per-token decay, and float32 y) use 32-byte
+    stores where a row starts 32-byte aligned and 16-byte stores elsewhere: through a view whose
+    row stride is 16 bytes past a multiple of 32 (rows alternate), the rows equal those written into a
+    contiguous y, and nothing around the view is touched."""
+    from prime_moment_attention_b200 import ops
+    q, k, v, ld, beta, st = _inputs()
+    qc, kc, vc, ldc, bc = q.cuda(), k.cuda(), v.cuda(), ld.cuda(), beta.cuda()
+    stc = tuple(t.cuda() for t in st)
+    width = D + (8 if out_dtype == torch.bfloat16 else 4)  # row stride 144 B (bf16) or 272 B (float32)
+    wide = torch.full((B, H, L, width), 7.0, dtype=out_dtype, device="cuda")
+    view = wide[:, :, :, :D]
+    if variant == "per_token_decay":
+        run = lambda y: ops.selective_prefill(qc, kc, vc, ldc, bc, state=stc, out_dtype=out_dtype, y_out=y)
+    else:
+        pst = ops.new_state(B, H, D, "cuda")
+        for a, b in zip(pst, st):
+            a.copy_(b.reshape(a.shape))
+        run = lambda y: ops.prefill(qc, kc, vc, 0.995, state=pst, out_dtype=out_dtype, y_out=y)
+    y_ref, _ = run(None)
+    run(view)
+    torch.cuda.synchronize()
+    assert torch.equal(view, y_ref)
+    assert bool((wide[..., D:] == 7.0).all())
